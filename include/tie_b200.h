@@ -1,0 +1,118 @@
+/* tie_b200.h -- additive entry points of the B200 GPT-2 engine.
+ *
+ * Nothing here replaces a reference declaration; these are the additions that
+ * the reference's single-sequence, host-logits API cannot express, listed in
+ * the reference's own terms:
+ *
+ *   - a greedy step that keeps the logits on the device and returns only the
+ *     argmax (the reference's greedy loop, src/main.c:274-287, copies a full
+ *     vocabulary row to the host every step and scans it there);
+ *   - batches of independent sequences sharing one model and one paged KV pool
+ *     (the reference has exactly one sequence per model, src/model.c:216-245);
+ *   - a whole greedy generation (prefill + every decode step) in one call, with
+ *     the token ids staying on the device between steps;
+ *   - access to the device and stream the model runs on, for callers that time
+ *     or order work around it.
+ *
+ * All functions validate their arguments before launching any work and return
+ * a model_status (include/model.h).
+ */
+#ifndef TIE_B200_TIE_H
+#define TIE_B200_TIE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* model_load onto an explicit CUDA device ordinal (model_load uses the
+ * calling thread's current device). */
+model_status model_load_on_device(const char *weights_path, const char *inventory_path,
+                                  const char *config_path, model_cproj_reading cproj_reading,
+                                  int device, model **out);
+
+/* The device ordinal and the cudaStream_t (as void*) every kernel of this model
+ * is launched on. */
+int   model_device(const model *m);
+void *model_stream(const model *m);
+
+/* Device bytes held by the weights (all layouts), and the number of kernels
+ * this library has launched for the model since load (graph replays count each
+ * node). */
+size_t   model_weight_device_bytes(const model *m);
+uint64_t model_kernel_launches(const model *m);
+
+/* Cached decode step at context n_ids (same preconditions as
+ * model_decode_step_cached) that returns only the greedy choice. */
+model_status model_decode_step_greedy(model *m, const int32_t *ids, size_t n_ids, int32_t *next_id);
+
+/* ---- batches of independent sequences --------------------------------------
+ * model_batch_reserve sizes a paged KV pool and scratch for n_seq sequences of
+ * up to `capacity` positions each (pages of KV_CACHE_PAGE_ROWS positions, page
+ * tables on the device). It is separate from the single-sequence cache of
+ * model_kv_reserve; the batch calls below use only the pool. */
+model_status model_batch_reserve(model *m, size_t n_seq, size_t capacity);
+
+/* Prefill of n_seq sequences of n_ids tokens each (ids: host, n_seq * n_ids,
+ * row-major). Writes every position's keys and values into the pool and sets
+ * each sequence's length to n_ids. logits_out (host, n_seq * n_ids * vocab
+ * floats, or NULL for none) receives all positions' logits; next_ids (host,
+ * n_seq, or NULL) receives each sequence's greedy choice at its last position. */
+model_status model_prefill_batch(model *m, const int32_t *ids, size_t n_seq, size_t n_ids,
+                                 float *logits_out, size_t logits_cap, int32_t *next_ids);
+
+/* One cached decode step for every sequence of the batch: token ids[s] is
+ * appended at sequence s's current length, which then grows by one. logits_out
+ * (host, n_seq * vocab floats, or NULL) and next_ids (host, n_seq, or NULL). */
+model_status model_decode_step_batch(model *m, const int32_t *ids, size_t n_seq,
+                                     float *logits_out, size_t logits_cap, int32_t *next_ids);
+
+/* Greedy generation: prefill of n_prompt tokens for each of n_seq sequences,
+ * then n_new greedy tokens each (n_new - 1 decode steps; the first new token
+ * comes from the prefill's last row), all on the device. prompts: host,
+ * n_seq * n_prompt; out_ids: host, n_seq * n_new. Requires a prior
+ * model_batch_reserve covering n_seq sequences of n_prompt + n_new - 1
+ * positions. The decode steps run as CUDA-graph replays. */
+model_status model_generate_greedy(model *m, const int32_t *prompts, size_t n_seq,
+                                   size_t n_prompt, size_t n_new, int32_t *out_ids);
+
+/* Device-resident variant for timing the kernels alone: prompts and out_ids are
+ * DEVICE buffers of the same shapes; no host copies, no synchronisation. */
+model_status model_generate_greedy_device(model *m, const int32_t *d_prompts, size_t n_seq,
+                                          size_t n_prompt, size_t n_new, int32_t *d_out_ids);
+
+/* ---- diagnostics --------------------------------------------------------
+ * Times `iters` back-to-back launches of one kernel of the forward pass, alone,
+ * on the model's stream with CUDA events, and stores the average milliseconds
+ * per launch (the numbers a roofline is computed from). It runs on the batch
+ * pool and scratch of model_batch_reserve, which must cover `rows` sequences of
+ * `context` positions, and overwrites their contents and the decode state.
+ *   TIE_KERNEL_DECODE_ATTENTION  one layer's decode attention (split + merge),
+ *                                `rows` sequences at context `context`
+ *   TIE_KERNEL_DECODE_QKV        the QKV matmul of a decode step, `rows` rows
+ *   TIE_KERNEL_DECODE_FC         the MLP up-projection (+ GELU) of a decode step
+ *   TIE_KERNEL_DECODE_MLP_PROJ   the MLP down-projection (+ residual)
+ *   TIE_KERNEL_DECODE_HEAD       the tied head with its fused argmax
+ *   TIE_KERNEL_PREFILL_ATTENTION causal attention over `context` tokens x `rows`
+ *   TIE_KERNEL_PREFILL_FC        the MLP up-projection over rows * context tokens */
+enum {
+    TIE_KERNEL_DECODE_ATTENTION = 0,
+    TIE_KERNEL_DECODE_QKV = 1,
+    TIE_KERNEL_DECODE_FC = 2,
+    TIE_KERNEL_DECODE_MLP_PROJ = 3,
+    TIE_KERNEL_DECODE_HEAD = 4,
+    TIE_KERNEL_PREFILL_ATTENTION = 5,
+    TIE_KERNEL_PREFILL_FC = 6
+};
+model_status model_time_kernel(model *m, int kernel, size_t rows, size_t context, int iters,
+                               float *avg_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIE_B200_TIE_H */

@@ -1,0 +1,114 @@
+"""Kernel-level parity on the GPU, through the C ABI (gemm.h and the LayerNorm
+entry point).  The naive matmul performs the reference's exact float operations,
+so it must match the CPU oracle BIT FOR BIT; the tiled kernels are compared with
+a float64 product at a stated tolerance."""
+import numpy as np
+import pytest
+
+import oracle
+import tie_b200
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def lcg(n, seed):
+    s, out = seed, np.empty(n, np.float32)
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        out[i] = np.float32((s >> 8) / 8388608.0 - 1.0)
+    return out
+
+
+def test_naive_hand_values():
+    """reference tests/test_gemm_naive.c:71-93"""
+    A = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    B = np.array([[7, 8], [9, 10], [11, 12]], np.float32)
+    assert tie_b200.gemm_naive(A, B).tolist() == [[58, 64], [139, 154]]
+    assert tie_b200.gemm_naive_bt(A, B.T.copy()).tolist() == [[58, 64], [139, 154]]
+
+
+def test_naive_identity_exact():
+    A = lcg(49, 12345).reshape(7, 7)
+    I = np.eye(7, dtype=np.float32)
+    assert np.array_equal(tie_b200.gemm_naive(A, I), A)
+    assert np.array_equal(tie_b200.gemm_naive(I, A), A)
+    assert np.array_equal(tie_b200.gemm_naive_bt(A, I), A)
+
+
+@pytest.mark.parametrize("M,K,N", [(5, 3, 8), (8, 3, 5), (8, 768, 768), (3, 3072, 768)])
+def test_naive_bit_exact_vs_oracle(M, K, N):
+    rng = np.random.default_rng(M * 1000 + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    assert np.array_equal(bits(tie_b200.gemm_naive(A, B)), bits(oracle.gemm_naive(A, B)))
+    Bt = B.T.copy()
+    assert np.array_equal(bits(tie_b200.gemm_naive_bt(A, Bt)), bits(oracle.gemm_naive_bt(A, Bt)))
+
+
+def test_naive_leading_dimensions_and_untouched_columns():
+    """reference tests/test_gemm_naive.c:146-167: a sub-block with ld > dims;
+    nothing outside the N columns of C is written."""
+    L = tie_b200.library()
+    M, K, N, LDA, LDB, LDC = 4, 3, 2, 11, 9, 7
+    A = lcg(M * LDA, 4242).reshape(M, LDA)
+    B = lcg(K * LDB, 99).reshape(K, LDB)
+    Cm = np.full((M, LDC), 12345.0, np.float32)
+    L.gemm_naive(M, N, K, A.ctypes.data, LDA, B.ctypes.data, LDB, Cm.ctypes.data, LDC)
+    ref = oracle.gemm_naive(np.ascontiguousarray(A[:, :K]), np.ascontiguousarray(B[:, :N]))
+    assert np.array_equal(bits(Cm[:, :N]), bits(ref))
+    assert np.all(Cm[:, N:] == 12345.0)
+
+
+def test_naive_empty_sum_writes_zero():
+    L = tie_b200.library()
+    A = np.array([[3.0]], np.float32)
+    Cm = np.array([[-1.0]], np.float32)
+    L.gemm_naive(1, 1, 0, A.ctypes.data, 1, A.ctypes.data, 1, Cm.ctypes.data, 1)
+    assert Cm[0, 0] == 0.0
+    Cm[0, 0] = 5.0
+    L.gemm_naive_bt(1, 1, 0, A.ctypes.data, 1, A.ctypes.data, 1, Cm.ctypes.data, 1)
+    assert Cm[0, 0] == 0.0
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 768, 2304), (7, 768, 3072), (130, 3072, 768),
+                                   (300, 768, 50257), (64, 1600, 4800), (9, 5, 3)])
+def test_tiled_bt_vs_float64(M, K, N):
+    rng = np.random.default_rng(M + K + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    Bt = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    got = tie_b200.gemm_tiled_bt(A, Bt)
+    ref = A.astype(np.float64) @ Bt.astype(np.float64).T
+    scale = np.abs(A).astype(np.float64) @ np.abs(Bt).astype(np.float64).T
+    # fp32 accumulation over K terms: |err| <= K * 2^-24 * sum|a||b| (loose bound)
+    assert np.all(np.abs(got - ref) <= K * 6e-8 * scale + 1e-30)
+
+
+def test_tiled_nn_and_batch_invariance():
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((200, 768)).astype(np.float32)
+    B = (rng.standard_normal((768, 640)) * 0.02).astype(np.float32)
+    full = tie_b200.gemm_tiled(A, B)
+    ref = A.astype(np.float64) @ B.astype(np.float64)
+    assert np.abs(full - ref).max() < 1e-4
+    # a row's result does not depend on the other rows of the batch
+    Bt = B.T.copy()
+    fullbt = tie_b200.gemm_tiled_bt(A, Bt)
+    for r in (0, 77, 199):
+        one = tie_b200.gemm_tiled_bt(A[r:r + 1], Bt)
+        assert np.array_equal(bits(one[0]), bits(fullbt[r]))
+
+
+def test_layernorm_normalize_device():
+    """reference tests/test_model.c:80-99 on the engine's LayerNorm kernel, and
+    agreement with the oracle's sequential double statistics to one ulp."""
+    x = lcg(768, 11) * np.float32(7.0) + np.float32(3.0)
+    y = tie_b200.layernorm_normalize(x, 1e-5)
+    yd = y.astype(np.float64)
+    assert abs(yd.mean()) < 1e-5 and abs(yd.var() - 1.0) < 1e-4
+    ref = oracle.layernorm_normalize(x, 1e-5)
+    ulps = np.abs(bits(y).astype(np.int64) - bits(ref).astype(np.int64))
+    assert ulps.max() <= 1

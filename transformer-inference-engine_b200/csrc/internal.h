@@ -1,0 +1,51 @@
+// internal.h -- structures shared by the host-side translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/kv_cache.h"
+#include "common.cuh"
+
+// The cache: per layer a key pool and a value pool of `rows` fp32 rows of
+// n_embd floats, all layers in one device allocation each. Pages of
+// KV_CACHE_PAGE_ROWS rows; sequence s's logical page p is physical page
+// page_table[s * pages_per_seq + p]. kv_cache_create builds a one-sequence
+// cache whose pages are in order, so each layer is one contiguous block of
+// `capacity` rows.
+struct kv_cache {
+    int n_layer = 0, n_embd = 0, capacity = 0, length = 0;
+    int n_seq = 1, pages_per_seq = 0;
+    size_t rows = 0;    // physical rows per layer
+    size_t bytes = 0;   // reported footprint
+    float* k = nullptr;
+    float* v = nullptr;
+    int* d_page_table = nullptr;
+};
+
+namespace tie {
+
+// A pool for n_seq sequences of up to `capacity` positions each.
+kv_status kv_pool_create(int n_layer, int n_embd, int n_seq, int capacity, kv_cache** out);
+
+inline PagedKV layer_view(const kv_cache* c, int layer) {
+    PagedKV v;
+    v.k = c->k + (size_t)layer * c->rows * c->n_embd;
+    v.v = c->v + (size_t)layer * c->rows * c->n_embd;
+    v.page_table = c->d_page_table;
+    v.pages_per_seq = c->pages_per_seq;
+    v.n_embd = c->n_embd;
+    return v;
+}
+
+// Copies n floats between any two of host/device memory and waits for it.
+cudaError_t copy_any(void* dst, const void* src, size_t bytes);
+
+cudaError_t launch_gemm_nn(const float* A, int lda, const float* B, int ldb, float* C, int ldc,
+                           int M, int N, int K, cudaStream_t st);
+
+}  // namespace tie

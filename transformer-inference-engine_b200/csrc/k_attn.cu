@@ -1,0 +1,348 @@
+// k_attn.cu -- causal attention for GPT-2 (head_dim 64), fp32.
+//
+// Prefill (reference model.c:705-732): per (sequence, head, 64-query tile) one
+// block streams 64-key tiles up to the diagonal through shared memory and keeps
+// an online softmax (running max and sum, rescaled accumulator); the T x T score
+// square is never materialised. Scores are q.k scaled by 1/sqrt(64), the
+// reference's order (dot product, then scale).
+//
+// Decode (reference model.c:826-850): one query per sequence against its cached
+// positions, read through the page table. Positions are split into 64-position
+// chunks, one block each (flash-decoding); a second kernel merges the chunk
+// partials (max, sum, unnormalised output) in chunk order.
+//
+// With statistics enabled (reference model_collect_attn_stats) a second pass
+// recomputes each row's normalised probabilities from the same scores and
+// records the min and max of their double-precision sums.
+#include "common.cuh"
+
+#include <cfloat>
+
+namespace tie {
+namespace {
+
+constexpr int D = 64;
+constexpr int BQ = 64, BKEY = 64, LDS = D + 4;
+constexpr int CH = 64;  // decode positions per split
+
+__device__ __forceinline__ void stats_update(AttnStats* st, double rowsum) {
+    const unsigned long long bits = (unsigned long long)__double_as_longlong(rowsum);
+    atomicMin(&st->min_bits, bits);
+    atomicMax(&st->max_bits, bits);
+    atomicAdd(&st->rows, 1ull);
+}
+
+// ------------------------------------------------------------------ prefill --
+template <bool STATS>
+__global__ void __launch_bounds__(128)
+attn_prefill_kernel(const float* __restrict__ qkv, int T, int H, float scale,
+                    float* __restrict__ out, AttnStats* stats) {
+    extern __shared__ __align__(16) float smem[];
+    float* Qs = smem;                  // [BQ][LDS]
+    float* Ks = Qs + BQ * LDS;         // [BKEY][LDS]
+    float* Vs = Ks + BKEY * LDS;       // [BKEY][LDS]
+    float* Pt = Vs + BKEY * LDS;       // [BKEY][BQ + 4], probabilities transposed
+
+    const int E = H * D, E3 = 3 * E;
+    // heavy (late) query tiles first
+    const int qt = gridDim.x - 1 - blockIdx.x;
+    const int h = blockIdx.y, seq = blockIdx.z;
+    const int q0 = qt * BQ;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ty = lane >> 3, tx = lane & 7;
+    const float* base = qkv + (size_t)seq * T * E3;
+
+    for (int i = tid; i < BQ * (D / 4); i += blockDim.x) {
+        const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q0 + r < T) v = *reinterpret_cast<const float4*>(base + (size_t)(q0 + r) * E3 + h * D + c);
+        *reinterpret_cast<float4*>(Qs + r * LDS + c) = v;
+    }
+
+    int rows[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rows[i] = warp * 16 + ty * 4 + i;
+    float m_i[4], l_i[4], o[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m_i[i] = -INFINITY;
+        l_i[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[i][d] = 0.f;
+    }
+
+    const int last_row = min(q0 + BQ, T) - 1;
+    const int n_kt = last_row / BKEY + 1;
+
+    auto load_kv = [&](int kt) {
+        for (int i = tid; i < BKEY * (D / 4); i += blockDim.x) {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            const int key = kt * BKEY + r;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (key < T) {
+                const float* p = base + (size_t)key * E3 + h * D + c;
+                kv = *reinterpret_cast<const float4*>(p + E);
+                vv = *reinterpret_cast<const float4*>(p + 2 * E);
+            }
+            *reinterpret_cast<float4*>(Ks + r * LDS + c) = kv;
+            *reinterpret_cast<float4*>(Vs + r * LDS + c) = vv;
+        }
+    };
+    // s[i][j]: row rows[i], key kt*BKEY + tx + 8*j
+    auto scores = [&](int kt, float (&s)[4][8]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < D; d += 4) {
+            float4 q[4], k[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + rows[i] * LDS + d);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (tx + 8 * j) * LDS + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float a = s[i][j];
+                    a = fmaf(q[i].x, k[j].x, a);
+                    a = fmaf(q[i].y, k[j].y, a);
+                    a = fmaf(q[i].z, k[j].z, a);
+                    a = fmaf(q[i].w, k[j].w, a);
+                    s[i][j] = a;
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int t = q0 + rows[i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int key = kt * BKEY + tx + 8 * j;
+                s[i][j] = key <= t ? s[i][j] * scale : -INFINITY;
+            }
+        }
+    };
+
+    for (int kt = 0; kt < n_kt; ++kt) {
+        __syncthreads();
+        load_kv(kt);
+        __syncthreads();
+        float s[4][8];
+        scores(kt, s);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mt = s[i][0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) mt = fmaxf(mt, s[i][j]);
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+            const float m_new = fmaxf(m_i[i], mt);
+            const float alpha = (m_i[i] == -INFINITY) ? 0.f : expf(m_i[i] - m_new);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float p = (s[i][j] == -INFINITY) ? 0.f : expf(s[i][j] - m_new);
+                Pt[(tx + 8 * j) * (BQ + 4) + rows[i]] = p;
+                ps += p;
+            }
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            l_i[i] = l_i[i] * alpha + ps;
+            m_i[i] = m_new;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[i][d] *= alpha;
+        }
+        __syncwarp();
+        const int kmax = min(BKEY, T - kt * BKEY);
+        for (int j = 0; j < kmax; ++j) {
+            const float4 p4 = *reinterpret_cast<const float4*>(Pt + j * (BQ + 4) + warp * 16 + ty * 4);
+            const float4 v0 = *reinterpret_cast<const float4*>(Vs + j * LDS + tx * 4);
+            const float4 v1 = *reinterpret_cast<const float4*>(Vs + j * LDS + 32 + tx * 4);
+            const float p[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                o[i][0] = fmaf(p[i], v0.x, o[i][0]);
+                o[i][1] = fmaf(p[i], v0.y, o[i][1]);
+                o[i][2] = fmaf(p[i], v0.z, o[i][2]);
+                o[i][3] = fmaf(p[i], v0.w, o[i][3]);
+                o[i][4] = fmaf(p[i], v1.x, o[i][4]);
+                o[i][5] = fmaf(p[i], v1.y, o[i][5]);
+                o[i][6] = fmaf(p[i], v1.z, o[i][6]);
+                o[i][7] = fmaf(p[i], v1.w, o[i][7]);
+            }
+        }
+        __syncwarp();
+    }
+
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = q0 + rows[i];
+        if (t < T) {
+            const float inv = 1.0f / l_i[i];
+            float* dst = out + ((size_t)seq * T + t) * E + h * D;
+            *reinterpret_cast<float4*>(dst + tx * 4) =
+                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+            *reinterpret_cast<float4*>(dst + 32 + tx * 4) =
+                make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+        }
+    }
+
+    if constexpr (STATS) {
+        // second pass: the normalised probabilities of each row, summed in double
+        // (reference softmax check, model.c:635-638)
+        double rs[4] = {0.0, 0.0, 0.0, 0.0};
+        float inv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) inv[i] = (float)(1.0 / (double)l_i[i]);
+        for (int kt = 0; kt < n_kt; ++kt) {
+            __syncthreads();
+            load_kv(kt);
+            __syncthreads();
+            float s[4][8];
+            scores(kt, s);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (s[i][j] != -INFINITY) rs[i] += (double)__fmul_rn(expf(s[i][j] - m_i[i]), inv[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 1);
+            rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 2);
+            rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 4);
+            if (tx == 0 && q0 + rows[i] < T) stats_update(stats, rs[i]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------- decode --
+// part layout per (b, h, split): [0] max, [1] sum, [2..2+D) unnormalised output
+constexpr int PART = D + 2;
+
+template <bool STATS>
+__global__ void __launch_bounds__(128)
+attn_decode_split_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int H,
+                         PagedKV kv, int max_splits, float scale, float* __restrict__ part,
+                         float* __restrict__ e_out, int e_ld) {
+    const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int ctx = lens[b] + 1;
+    const int p0 = s * CH;
+    if (p0 >= ctx) return;
+    const int n = min(CH, ctx - p0);
+    const int E = kv.n_embd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float s_e[CH];
+    __shared__ float s_o[2][D];
+
+    const float2 q = *reinterpret_cast<const float2*>(qkv + (size_t)b * 3 * E + h * D + 2 * lane);
+    for (int i = warp; i < n; i += 4) {
+        const size_t row = kv.row(b, p0 + i);
+        const float2 k = *reinterpret_cast<const float2*>(kv.k + row * E + h * D + 2 * lane);
+        float a = fmaf(q.x, k.x, q.y * k.y);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) s_e[i] = a * scale;
+    }
+    __syncthreads();
+    float mx = s_e[0];
+    for (int i = 1; i < n; ++i) mx = fmaxf(mx, s_e[i]);
+    __syncthreads();
+    if (tid < n) s_e[tid] = expf(s_e[tid] - mx);
+    __syncthreads();
+    float l = 0.f;
+    for (int i = 0; i < n; ++i) l += s_e[i];
+
+    const int d = tid & (D - 1), half = tid >> 6;
+    float acc = 0.f;
+    for (int i = half; i < n; i += 2) {
+        const size_t row = kv.row(b, p0 + i);
+        acc = fmaf(s_e[i], kv.v[row * E + h * D + d], acc);
+    }
+    s_o[half][d] = acc;
+    __syncthreads();
+    float* pp = part + ((size_t)(b * H + h) * max_splits + s) * PART;
+    if (tid < D) pp[2 + tid] = s_o[0][tid] + s_o[1][tid];
+    if (tid == 0) { pp[0] = mx; pp[1] = l; }
+    if constexpr (STATS) {
+        if (tid < n) e_out[(size_t)(b * H + h) * e_ld + p0 + tid] = s_e[tid];
+    }
+}
+
+template <bool STATS>
+__global__ void __launch_bounds__(D)
+attn_decode_combine_kernel(const int32_t* __restrict__ lens, int H, int max_splits,
+                           const float* __restrict__ part, float* __restrict__ out,
+                           const float* __restrict__ e_in, int e_ld, AttnStats* stats) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int ctx = lens[b] + 1;
+    const int ns = (ctx + CH - 1) / CH;
+    const float* pp = part + (size_t)(b * H + h) * max_splits * PART;
+    float m = pp[0];
+    for (int s = 1; s < ns; ++s) m = fmaxf(m, pp[s * PART]);
+    float l = 0.f, o = 0.f;
+    for (int s = 0; s < ns; ++s) {
+        const float c = expf(pp[s * PART] - m);
+        l = fmaf(pp[s * PART + 1], c, l);
+        o = fmaf(pp[s * PART + 2 + d], c, o);
+    }
+    out[(size_t)b * H * D + h * D + d] = o / l;
+    if constexpr (STATS) {
+        if (d == 0) {
+            const float inv = (float)(1.0 / (double)l);
+            double rs = 0.0;
+            for (int s = 0; s < ns; ++s) {
+                const float c = expf(pp[s * PART] - m);
+                const int n = min(CH, ctx - s * CH);
+                for (int i = 0; i < n; ++i)
+                    rs += (double)__fmul_rn(__fmul_rn(e_in[(size_t)(b * H + h) * e_ld + s * CH + i], c), inv);
+            }
+            stats_update(stats, rs);
+        }
+    }
+}
+
+}  // namespace
+
+int attn_decode_max_splits(int capacity) { return (capacity + CH - 1) / CH; }
+
+cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
+                                AttnStats* stats, cudaStream_t st) {
+    if (T <= 0 || n_seq <= 0) return cudaSuccess;
+    const size_t smem = (size_t)(BQ * LDS * 3 + BKEY * (BQ + 4)) * sizeof(float);
+    const float scale = (float)(1.0 / sqrt((double)D));
+    dim3 grid((T + BQ - 1) / BQ, H, n_seq);
+    if (stats) {
+        cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_prefill_kernel<true><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, stats);
+    } else {
+        cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_prefill_kernel<false><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, nullptr);
+    }
+    return cudaGetLastError();
+}
+
+// part: B * H * max_splits * (D + 2) floats. With stats, `part` must also hold
+// B * H * max_splits * CH floats after the partials for the probabilities.
+cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv,
+                               int max_splits, float* part, float* out, AttnStats* stats,
+                               cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    const float scale = (float)(1.0 / sqrt((double)D));
+    dim3 g1(max_splits, H, B), g2(H, B);
+    if (stats) {
+        float* e = part + (size_t)B * H * max_splits * PART;
+        const int e_ld = max_splits * CH;
+        attn_decode_split_kernel<true><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, e, e_ld);
+        attn_decode_combine_kernel<true><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, e, e_ld, stats);
+    } else {
+        attn_decode_split_kernel<false><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, nullptr, 0);
+        attn_decode_combine_kernel<false><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, nullptr, 0, nullptr);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace tie

@@ -1,0 +1,334 @@
+// k_misc.cu -- embedding, LayerNorm, KV stores, argmax reductions, greedy-step
+// bookkeeping, the load-time transpose and the naive (reference-order) matmul.
+#include "common.cuh"
+
+#include <cfloat>
+#include <climits>
+
+namespace tie {
+
+namespace {
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------- embedding --
+// model.c:671-676 / 805-809: x = wte[id] + wpe[pos], one float add per element.
+// An id outside [0, V) (only possible through the device-buffer entry point,
+// whose ids the host cannot check) yields a NaN row instead of a wild read.
+__global__ void embed_prefill_kernel(const int32_t* __restrict__ ids, int rows, int T,
+                                     const float* __restrict__ wte,
+                                     const float* __restrict__ wpe, float* __restrict__ x,
+                                     int E, int V) {
+    const int E4 = E >> 2;
+    const long long n = (long long)rows * E4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / E4), c = (int)(i % E4);
+        const int t = r % T;
+        const int id = ids[r];
+        if ((unsigned)id >= (unsigned)V) {
+            reinterpret_cast<float4*>(x + (size_t)r * E)[c] = make_float4(NAN, NAN, NAN, NAN);
+            continue;
+        }
+        const float4 a = reinterpret_cast<const float4*>(wte + (size_t)id * E)[c];
+        const float4 b = reinterpret_cast<const float4*>(wpe + (size_t)t * E)[c];
+        reinterpret_cast<float4*>(x + (size_t)r * E)[c] =
+            make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                        __fadd_rn(a.w, b.w));
+    }
+}
+
+__global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
+                                    const int32_t* __restrict__ lens, int B,
+                                    const float* __restrict__ wte,
+                                    const float* __restrict__ wpe, float* __restrict__ x, int E, int V) {
+    const int E4 = E >> 2;
+    const int n = B * E4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int b = i / E4, c = i % E4;
+        const int id = tokens[b];
+        if ((unsigned)id >= (unsigned)V) {
+            reinterpret_cast<float4*>(x + (size_t)b * E)[c] = make_float4(NAN, NAN, NAN, NAN);
+            continue;
+        }
+        const float4 a = reinterpret_cast<const float4*>(wte + (size_t)id * E)[c];
+        const float4 p = reinterpret_cast<const float4*>(wpe + (size_t)lens[b] * E)[c];
+        reinterpret_cast<float4*>(x + (size_t)b * E)[c] =
+            make_float4(__fadd_rn(a.x, p.x), __fadd_rn(a.y, p.y), __fadd_rn(a.z, p.z),
+                        __fadd_rn(a.w, p.w));
+    }
+}
+
+// ------------------------------------------------------------- LayerNorm --
+// model.c:593-610: mean and biased variance in double, inv = (float)(1/sqrt(var
+// + eps)), normalized = (float)((x - mean) * inv), then a float multiply by the
+// gain and a float add of the shift, each rounded separately. One warp per row.
+__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                 const float* __restrict__ bvec, float* __restrict__ y,
+                                 int rows, int E, float eps) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + (size_t)row * E;
+    double s = 0.0;
+    for (int i = lane; i < E; i += 32) s = __dadd_rn(s, (double)xr[i]);
+    s = warp_sum_d(s);
+    const double mean = s / (double)E;
+    double v = 0.0;
+    for (int i = lane; i < E; i += 32) {
+        const double d = __dadd_rn((double)xr[i], -mean);
+        v = __dadd_rn(v, __dmul_rn(d, d));
+    }
+    v = warp_sum_d(v);
+    v = v / (double)E;
+    const float inv = (float)(1.0 / sqrt(__dadd_rn(v, (double)eps)));
+    float* yr = y + (size_t)row * E;
+    for (int i = lane; i < E; i += 32) {
+        const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
+        yr[i] = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
+    }
+}
+
+// ------------------------------------------------------------- KV stores --
+__global__ void kv_store_prefill_kernel(const float* __restrict__ qkv, int n_seq, int T,
+                                        PagedKV kv, int first_seq) {
+    const int E = kv.n_embd, E4 = E >> 2;
+    const long long n = (long long)n_seq * T * E4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(i % E4);
+        const long long r = i / E4;
+        const int t = (int)(r % T), s = (int)(r / T);
+        const float4* src = reinterpret_cast<const float4*>(qkv + (size_t)r * 3 * E);
+        const size_t row = kv.row(first_seq + s, t);
+        reinterpret_cast<float4*>(kv.k + row * E)[c] = src[E4 + c];
+        reinterpret_cast<float4*>(kv.v + row * E)[c] = src[2 * E4 + c];
+    }
+}
+
+__global__ void kv_store_decode_kernel(const float* __restrict__ qkv,
+                                       const int32_t* __restrict__ lens, int B, PagedKV kv) {
+    const int E = kv.n_embd, E4 = E >> 2;
+    const int n = B * E4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int b = i / E4, c = i % E4;
+        const float4* src = reinterpret_cast<const float4*>(qkv + (size_t)b * 3 * E);
+        const size_t row = kv.row(b, lens[b]);
+        reinterpret_cast<float4*>(kv.k + row * E)[c] = src[E4 + c];
+        reinterpret_cast<float4*>(kv.v + row * E)[c] = src[2 * E4 + c];
+    }
+}
+
+// -------------------------------------------------------------- argmax --
+// Candidates (value, index); index -1 means "none yet". A candidate beats the
+// current best when it is larger, or equal with a lower index: the result of
+// the reference's strict '>' scan from index 0 (model.c:920-925). NaN values
+// never become candidates; a partial whose range starts with a NaN at index 0
+// reports index -2, which makes the final answer 0 (the scan never moves off
+// index 0 when v[0] is NaN).
+__device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
+    return bi < 0 || v > bv || (v == bv && i < bi);
+}
+
+__global__ void argmax_finalize_kernel(const float* __restrict__ pv, const int* __restrict__ pi,
+                                       int n_parts, int M, int32_t* __restrict__ next) {
+    const int m = blockIdx.x;
+    if (m >= M) return;
+    float bv = 0.f;
+    int bi = -1;
+    bool nan0 = false;
+    for (int p = threadIdx.x; p < n_parts; p += blockDim.x) {
+        const int i = pi[(size_t)p * M + m];
+        const float v = pv[(size_t)p * M + m];
+        if (i == -2) nan0 = true;
+        else if (i >= 0 && beats(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int snan;
+    if (threadIdx.x == 0) snan = 0;
+    __syncthreads();
+    if (nan0) atomicOr(&snan, 1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && beats(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (si[k] >= 0 && beats(sv[k], si[k], bv, bi)) { bv = sv[k]; bi = si[k]; }
+        next[m] = snan ? 0 : (bi < 0 ? 0 : bi);
+    }
+}
+
+// argmax of full rows of a logits matrix: row b = row_offset + b * row_stride
+__global__ void argmax_rows_kernel(const float* __restrict__ L, int ldl, int N, int row_stride,
+                                   int row_offset, int32_t* __restrict__ next) {
+    const int b = blockIdx.x;
+    const float* r = L + (size_t)(row_offset + (size_t)b * row_stride) * ldl;
+    float bv = 0.f;
+    int bi = -1;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const float v = r[i];
+        if (v == v && beats(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && beats(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (si[k] >= 0 && beats(sv[k], si[k], bv, bi)) { bv = sv[k]; bi = si[k]; }
+        const bool nan0 = !(r[0] == r[0]);
+        next[b] = nan0 ? 0 : (bi < 0 ? 0 : bi);
+    }
+}
+
+// ----------------------------------------------------- greedy bookkeeping --
+__global__ void step_advance_kernel(const int32_t* __restrict__ next, int32_t* __restrict__ tokens,
+                                    int32_t* __restrict__ lens, int32_t* __restrict__ out,
+                                    int ld_out, int32_t* __restrict__ step, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    const int s = *step;
+    __syncthreads();
+    if (b < B) {
+        const int32_t t = next[b];
+        tokens[b] = t;
+        out[(size_t)b * ld_out + s] = t;
+        lens[b] += 1;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *step = s + 1;
+}
+
+// ------------------------------------------------------------ transpose --
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int R,
+                                 int Cc) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < R && c < Cc) tile[i][threadIdx.x] = in[(size_t)r * Cc + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < R && c < Cc) out[(size_t)c * R + r] = tile[threadIdx.x][i];
+    }
+}
+
+// ---------------------------------------------------------- naive matmul --
+// gemm_naive.c:30-60 on the device: one thread per output, one accumulator,
+// k ascending, product and sum rounded separately (no fused multiply-add).
+__global__ void gemm_naive_kernel(int M, int N, int K, const float* __restrict__ A, int lda,
+                                  const float* __restrict__ B, int ldb, float* __restrict__ C,
+                                  int ldc, int bt) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.y;
+    if (i >= M || j >= N) return;
+    float acc = 0.0f;
+    const float* a = A + (size_t)i * lda;
+    if (bt) {
+        const float* b = B + (size_t)j * ldb;
+        for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __fmul_rn(a[k], b[k]));
+    } else {
+        for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __fmul_rn(a[k], B[(size_t)k * ldb + j]));
+    }
+    C[(size_t)i * ldc + j] = acc;
+}
+
+inline int grid_for(long long n, int block) {
+    long long g = (n + block - 1) / block;
+    if (g > 148 * 32) g = 148 * 32;
+    return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+cudaError_t launch_embed_prefill(const int32_t* ids, int rows, int T, const float* wte,
+                                 const float* wpe, float* x, int E, int V, cudaStream_t st) {
+    embed_prefill_kernel<<<grid_for((long long)rows * (E / 4), 256), 256, 0, st>>>(ids, rows, T,
+                                                                                    wte, wpe, x, E, V);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed_decode(const int32_t* tokens, const int32_t* lens, int B,
+                                const float* wte, const float* wpe, float* x, int E, int V,
+                                cudaStream_t st) {
+    embed_decode_kernel<<<grid_for((long long)B * (E / 4), 256), 256, 0, st>>>(tokens, lens, B,
+                                                                                wte, wpe, x, E, V);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float* y, int rows,
+                             int E, float eps, cudaStream_t st) {
+    const int warps_per_block = 8;
+    const int grid = (rows + warps_per_block - 1) / warps_per_block;
+    layernorm_kernel<<<grid, warps_per_block * 32, 0, st>>>(x, g, b, y, rows, E, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_store_prefill(const float* qkv, int n_seq, int T, PagedKV kv, int first_seq,
+                                    cudaStream_t st) {
+    kv_store_prefill_kernel<<<grid_for((long long)n_seq * T * (kv.n_embd / 4), 256), 256, 0, st>>>(
+        qkv, n_seq, T, kv, first_seq);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_store_decode(const float* qkv, const int32_t* lens, int B, PagedKV kv,
+                                   cudaStream_t st) {
+    kv_store_decode_kernel<<<grid_for((long long)B * (kv.n_embd / 4), 256), 256, 0, st>>>(
+        qkv, lens, B, kv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_finalize(const float* part_val, const int* part_idx, int n_parts, int M,
+                                   int32_t* next, cudaStream_t st) {
+    argmax_finalize_kernel<<<M, 256, 0, st>>>(part_val, part_idx, n_parts, M, next);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows(const float* L, int ldl, int M, int N, int row_stride,
+                               int row_offset, int32_t* next, cudaStream_t st) {
+    argmax_rows_kernel<<<M, 512, 0, st>>>(L, ldl, N, row_stride, row_offset, next);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step_advance(const int32_t* next, int32_t* tokens, int32_t* lens,
+                                int32_t* out, int ld_out, int32_t* step, int B, cudaStream_t st) {
+    // One block: every thread reads *step before thread 0 advances it.
+    if (B > 1024) return cudaErrorInvalidValue;
+    step_advance_kernel<<<1, 1024, 0, st>>>(next, tokens, lens, out, ld_out, step, B);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose(const float* in, float* out, int R, int Cc, cudaStream_t st) {
+    dim3 grid((Cc + 31) / 32, (R + 31) / 32);
+    transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(in, out, R, Cc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_naive(int M, int N, int K, const float* A, int lda, const float* B,
+                              int ldb, float* C, int ldc, bool bt, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (M > 65535) return cudaErrorInvalidValue;
+    dim3 grid((N + 127) / 128, M);
+    gemm_naive_kernel<<<grid, 128, 0, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bt ? 1 : 0);
+    return cudaGetLastError();
+}
+
+}  // namespace tie

@@ -1,0 +1,1144 @@
+// model.cu -- the model_* C ABI (include/model.h, include/tie_b200.h) on one B200.
+//
+// Host orchestration only: argument checks in the reference's order, the
+// load-time upload of the weights to device memory, scratch management, and the
+// launch sequence of the forward pass. Every arithmetic step of the token loop
+// is a kernel (k_*.cu).
+//
+// Reference correspondence (src/model.c):
+//   model_load            331-467   config + inventory + weight file, cross-checked
+//   model_reserve         566-589   device scratch instead of host scratch
+//   forward (prefill)     647-763   launch sequence in run_prefill()
+//   cached decode         794-868   launch sequence in run_decode()
+//   model_prefill         765-782, model_decode_step_cached 870-896,
+//   model_decode_step     898-918, model_argmax 920-925
+#include "../../include/model.h"
+#include "../../include/safetensors.h"
+#include "../../include/tie_b200.h"
+#include "internal.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <vector>
+
+using namespace tie;
+
+namespace {
+
+// ------------------------------------------------------------------ JSON --
+// Just enough to read the two flat, machine-written artifacts: find "key", then
+// ':' and read the value. Mirrors what the reference's loader reads
+// (model.c:87-133), written afresh.
+const char* after_key(const char* s, const char* key) {
+    std::string pat = std::string("\"") + key + "\"";
+    const char* p = std::strstr(s, pat.c_str());
+    if (!p) return nullptr;
+    p += pat.size();
+    while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') ++p;
+    if (*p != ':') return nullptr;
+    ++p;
+    while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') ++p;
+    return p;
+}
+
+bool json_num(const char* s, const char* key, double* out) {
+    const char* p = after_key(s, key);
+    if (!p) return false;
+    char* end = nullptr;
+    const double v = std::strtod(p, &end);
+    if (end == p) return false;
+    *out = v;
+    return true;
+}
+
+bool json_int(const char* s, const char* key, int* out) {
+    double v;
+    if (!json_num(s, key, &v)) return false;
+    *out = (int)v;
+    return true;
+}
+
+bool json_str(const char* s, const char* key, char* out, size_t cap) {
+    const char* p = after_key(s, key);
+    if (!p || *p != '"') return false;
+    ++p;
+    size_t i = 0;
+    while (*p && *p != '"') {
+        if (i + 1 >= cap) return false;
+        out[i++] = *p++;
+    }
+    if (*p != '"') return false;
+    out[i] = 0;
+    return true;
+}
+
+bool read_text(const char* path, std::string* out) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return false;
+    std::fseek(f, 0, SEEK_END);
+    long n = std::ftell(f);
+    if (n < 0) { std::fclose(f); return false; }
+    std::rewind(f);
+    out->resize((size_t)n);
+    size_t got = n ? std::fread(&(*out)[0], 1, (size_t)n, f) : 0;
+    out->resize(got);
+    std::fclose(f);
+    return true;
+}
+
+// One inventory record: the line that starts with {"name": "<name>",
+struct InvEntry {
+    char dtype[16] = {0};
+    char orientation[48] = {0};
+    int n_dims = 0;
+    long long dims[8] = {0};
+    unsigned long long file_offset = 0, nbytes = 0;
+};
+
+bool inventory_find(const std::string& inv, const char* name, InvEntry* e) {
+    std::string pat = std::string("{\"name\": \"") + name + "\",";
+    size_t at = inv.find(pat);
+    if (at == std::string::npos) return false;
+    size_t eol = inv.find('\n', at);
+    std::string line = inv.substr(at, eol == std::string::npos ? std::string::npos : eol - at);
+    *e = InvEntry();
+    if (!json_str(line.c_str(), "dtype", e->dtype, sizeof e->dtype)) return false;
+    if (!json_str(line.c_str(), "orientation", e->orientation, sizeof e->orientation)) return false;
+    double v;
+    if (!json_num(line.c_str(), "file_offset", &v)) return false;
+    e->file_offset = (unsigned long long)v;
+    if (!json_num(line.c_str(), "nbytes", &v)) return false;
+    e->nbytes = (unsigned long long)v;
+    const char* sh = after_key(line.c_str(), "shape");
+    if (!sh || *sh != '[') return false;
+    ++sh;
+    while (*sh && *sh != ']') {
+        while (*sh == ' ' || *sh == ',') ++sh;
+        if (*sh == ']') break;
+        char* end = nullptr;
+        long long d = std::strtoll(sh, &end, 10);
+        if (end == sh || e->n_dims >= 8) return false;
+        e->dims[e->n_dims++] = d;
+        sh = end;
+    }
+    return true;
+}
+
+struct Layer {
+    float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
+    float *ln2_w, *ln2_b, *fc_w, *fc_b, *mlp_w, *mlp_b;
+};
+
+// One instantiated decode graph per (batch size, cache, advance, output) key,
+// with the number of kernels one replay runs.
+struct GraphKey {
+    int B;
+    const kv_cache* cache;
+    bool advance;
+    const int32_t* out;
+    int ld_out;
+    bool operator<(const GraphKey& o) const {
+        if (B != o.B) return B < o.B;
+        if (cache != o.cache) return cache < o.cache;
+        if (advance != o.advance) return advance < o.advance;
+        if (out != o.out) return out < o.out;
+        return ld_out < o.ld_out;
+    }
+};
+struct GraphEntry {
+    cudaGraphExec_t exec;
+    uint64_t kernels;
+};
+
+}  // namespace
+
+struct model {
+    model_config cfg{};
+    model_cproj_reading cproj = MODEL_CPROJ_AS_STORED;
+    model_decode_path path = MODEL_PATH_NOCACHE;
+    kv_cache* kv = nullptr;
+    const gemm_impl* gemm_choice = &gemm_impl_sm100a;
+    int device = 0;
+    cudaStream_t st = nullptr;
+
+    float* d_weights = nullptr;
+    size_t weight_bytes = 0;
+    float *wte = nullptr, *wpe = nullptr, *lnf_w = nullptr, *lnf_b = nullptr;
+    std::vector<Layer> layers;
+    std::vector<model_tensor_record> records;
+
+    // activation scratch: `rows` rows
+    size_t rows = 0;
+    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr;
+    size_t logit_rows = 0;
+    float* logits = nullptr;
+    size_t ids_cap = 0;
+    int32_t* d_ids = nullptr;
+
+    // decode state (batch slots)
+    size_t slots = 0;
+    int32_t *d_tokens = nullptr, *d_lens = nullptr, *d_next = nullptr, *d_step = nullptr;
+    size_t out_cap = 0;
+    int32_t* d_out = nullptr;
+    size_t part_floats = 0;
+    float* d_part = nullptr;
+    size_t am_parts = 0;
+    float* d_am_val = nullptr;
+    int* d_am_idx = nullptr;
+
+    // pinned staging for small host<->device transfers
+    int32_t* h_small = nullptr;
+    size_t h_small_cap = 0;
+
+    bool stats_on = false;
+    AttnStats* d_stats = nullptr;
+    double rs_min = 0.0, rs_max = 0.0;
+    size_t rs_rows = 0;
+
+    kv_cache* pool = nullptr;
+    std::map<GraphKey, GraphEntry> graphs;
+    uint64_t launches = 0;
+};
+
+namespace {
+
+#define CU(expr)                                                   \
+    do {                                                           \
+        cudaError_t e_ = (expr);                                   \
+        if (e_ != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; } \
+    } while (0)
+
+#define LAUNCH(expr)                                               \
+    do {                                                           \
+        cudaError_t e_ = (expr);                                   \
+        ++m->launches;                                             \
+        if (e_ != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; } \
+    } while (0)
+
+void drop_graphs(model* m) {
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second.exec);
+    m->graphs.clear();
+}
+
+template <typename T>
+model_status grow(T** p, size_t* cap, size_t need) {
+    if (need <= *cap) return MODEL_OK;
+    T* fresh = nullptr;
+    if (cudaMalloc(&fresh, need * sizeof(T)) != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_NOMEM; }
+    cudaFree(*p);
+    *p = fresh;
+    *cap = need;
+    return MODEL_OK;
+}
+
+model_status ensure_rows(model* m, size_t rows) {
+    if (rows <= m->rows) return MODEL_OK;
+    drop_graphs(m);
+    const size_t E = (size_t)m->cfg.n_embd;
+    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr;
+    if (cudaMalloc(&x, rows * E * 4) != cudaSuccess || cudaMalloc(&xb, rows * E * 4) != cudaSuccess ||
+        cudaMalloc(&qkv, rows * 3 * E * 4) != cudaSuccess ||
+        cudaMalloc(&attn, rows * E * 4) != cudaSuccess ||
+        cudaMalloc(&ff, rows * 4 * E * 4) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(x); cudaFree(xb); cudaFree(qkv); cudaFree(attn); cudaFree(ff);
+        return MODEL_ERR_NOMEM;
+    }
+    cudaFree(m->x); cudaFree(m->xb); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->ff);
+    m->x = x; m->xb = xb; m->qkv = qkv; m->attn = attn; m->ff = ff;
+    m->rows = rows;
+    return grow(&m->d_ids, &m->ids_cap, rows);
+}
+
+model_status ensure_logits(model* m, size_t rows) {
+    if (rows <= m->logit_rows) return MODEL_OK;
+    drop_graphs(m);
+    size_t cap = m->logit_rows * (size_t)m->cfg.vocab_size;
+    model_status rc = grow(&m->logits, &cap, rows * (size_t)m->cfg.vocab_size);
+    if (rc == MODEL_OK) m->logit_rows = rows;
+    return rc;
+}
+
+model_status ensure_pinned(model* m, size_t n_ints) {
+    if (n_ints <= m->h_small_cap) return MODEL_OK;
+    int32_t* p = nullptr;
+    if (cudaMallocHost(&p, n_ints * sizeof(int32_t)) != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_NOMEM; }
+    cudaFreeHost(m->h_small);
+    m->h_small = p;
+    m->h_small_cap = n_ints;
+    return MODEL_OK;
+}
+
+// Decode-state buffers for B sequences with a cache of `capacity` positions.
+model_status ensure_slots(model* m, size_t B, int capacity) {
+    model_status rc = ensure_rows(m, B);
+    if (rc != MODEL_OK) return rc;
+    if (B > m->slots) {
+        drop_graphs(m);
+        size_t c1 = m->slots, c2 = m->slots, c3 = m->slots;
+        if ((rc = grow(&m->d_tokens, &c1, B)) != MODEL_OK) return rc;
+        if ((rc = grow(&m->d_lens, &c2, B)) != MODEL_OK) return rc;
+        if ((rc = grow(&m->d_next, &c3, B)) != MODEL_OK) return rc;
+        m->slots = B;
+    }
+    if (!m->d_step) CU(cudaMalloc(&m->d_step, sizeof(int32_t)));
+    if (!m->d_stats) CU(cudaMalloc(&m->d_stats, sizeof(AttnStats)));
+    const size_t splits = (size_t)attn_decode_max_splits(capacity);
+    const size_t need = B * (size_t)m->cfg.n_head * splits * (64 + 2 + 64);
+    if (need > m->part_floats) {
+        drop_graphs(m);
+        if ((rc = grow(&m->d_part, &m->part_floats, need)) != MODEL_OK) return rc;
+    }
+    const size_t parts = (size_t)gemv_argmax_blocks(m->cfg.vocab_size) * B;
+    if (parts > m->am_parts) {
+        drop_graphs(m);
+        size_t c1 = m->am_parts, c2 = m->am_parts;
+        if ((rc = grow(&m->d_am_val, &c1, parts)) != MODEL_OK) return rc;
+        if ((rc = grow(&m->d_am_idx, &c2, parts)) != MODEL_OK) return rc;
+        m->am_parts = parts;
+    }
+    if ((rc = ensure_logits(m, B)) != MODEL_OK) return rc;
+    return ensure_pinned(m, 2 * B + 16);
+}
+
+// ------------------------------------------------------------- stats --
+model_status stats_begin(model* m) {
+    if (!m->stats_on) return MODEL_OK;
+    if (!m->d_stats) CU(cudaMalloc(&m->d_stats, sizeof(AttnStats)));
+    AttnStats init{~0ull, 0ull, 0ull};
+    CU(cudaMemcpyAsync(m->d_stats, &init, sizeof init, cudaMemcpyHostToDevice, m->st));
+    CU(cudaStreamSynchronize(m->st));
+    return MODEL_OK;
+}
+
+model_status stats_end(model* m) {
+    if (!m->stats_on) return MODEL_OK;
+    AttnStats s;
+    CU(cudaMemcpy(&s, m->d_stats, sizeof s, cudaMemcpyDeviceToHost));
+    if (s.rows) {
+        double lo, hi;
+        std::memcpy(&lo, &s.min_bits, 8);
+        std::memcpy(&hi, &s.max_bits, 8);
+        if (m->rs_rows == 0) { m->rs_min = lo; m->rs_max = hi; }
+        else {
+            if (lo < m->rs_min) m->rs_min = lo;
+            if (hi > m->rs_max) m->rs_max = hi;
+        }
+        m->rs_rows += (size_t)s.rows;
+    }
+    return MODEL_OK;
+}
+
+// --------------------------------------------------------- forward passes --
+// Prefill of n_seq sequences of T tokens whose ids are in m->d_ids; leaves
+// LN_f(x) in m->xb. Keys and values go to `cache` when it is non-NULL
+// (sequences first_seq..).                                   model.c:647-763
+model_status run_prefill(model* m, int n_seq, int T, kv_cache* cache, int first_seq) {
+    const int E = m->cfg.n_embd, H = m->cfg.n_head, R = n_seq * T;
+    const float eps = m->cfg.layer_norm_epsilon;
+    cudaStream_t st = m->st;
+    AttnStats* stats = m->stats_on ? m->d_stats : nullptr;
+    LAUNCH(launch_embed_prefill(m->d_ids, R, T, m->wte, m->wpe, m->x, E, m->cfg.vocab_size, st));
+    for (int l = 0; l < m->cfg.n_layer; ++l) {
+        const Layer& w = m->layers[l];
+        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, m->xb, R, E, eps, st));
+        LAUNCH(launch_gemm_tn(m->xb, E, w.qkv_w, E, w.qkv_b, m->qkv, 3 * E, R, 3 * E, E, EPI_BIAS, st));
+        if (cache) LAUNCH(launch_kv_store_prefill(m->qkv, n_seq, T, layer_view(cache, l), first_seq, st));
+        LAUNCH(launch_attn_prefill(m->qkv, n_seq, T, H, m->attn, stats, st));
+        LAUNCH(launch_gemm_tn(m->attn, E, w.proj_w, E, w.proj_b, m->x, E, R, E, E, EPI_BIAS_RESID, st));
+        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, R, E, eps, st));
+        LAUNCH(launch_gemm_tn(m->xb, E, w.fc_w, E, w.fc_b, m->ff, 4 * E, R, 4 * E, E, EPI_BIAS_GELU, st));
+        LAUNCH(launch_gemm_tn(m->ff, 4 * E, w.mlp_w, 4 * E, w.mlp_b, m->x, E, R, E, 4 * E, EPI_BIAS_RESID, st));
+    }
+    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, R, E, eps, st));
+    return MODEL_OK;
+}
+
+// One decode step for B sequences: token d_tokens[b] at position d_lens[b],
+// attending over positions 0..d_lens[b] of `cache`; logits of the step into
+// m->logits [B, V] and the greedy choice into d_next.          model.c:794-868
+// Everything it reads from the host side is fixed at capture time, so the
+// sequence can be recorded once and replayed as a graph.
+model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
+    const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size;
+    const float eps = m->cfg.layer_norm_epsilon;
+    cudaStream_t st = m->st;
+    AttnStats* stats = m->stats_on ? m->d_stats : nullptr;
+    const int max_splits = attn_decode_max_splits(cache->capacity);
+    const bool small = B <= 16;
+    auto mm = [&](const float* X, int ldx, const float* Wt, const float* bias, float* Y, int ldy,
+                  int N, int K, int epi) -> cudaError_t {
+        return small ? launch_gemv(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st)
+                     : launch_gemm_tn(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st);
+    };
+    LAUNCH(launch_embed_decode(m->d_tokens, m->d_lens, B, m->wte, m->wpe, m->x, E, V, st));
+    for (int l = 0; l < m->cfg.n_layer; ++l) {
+        const Layer& w = m->layers[l];
+        const PagedKV view = layer_view(cache, l);
+        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, m->xb, B, E, eps, st));
+        LAUNCH(mm(m->xb, E, w.qkv_w, w.qkv_b, m->qkv, 3 * E, 3 * E, E, EPI_BIAS));
+        LAUNCH(launch_kv_store_decode(m->qkv, m->d_lens, B, view, st));
+        LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st));
+        ++m->launches;  // the combine kernel
+        LAUNCH(mm(m->attn, E, w.proj_w, w.proj_b, m->x, E, E, E, EPI_BIAS_RESID));
+        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, B, E, eps, st));
+        LAUNCH(mm(m->xb, E, w.fc_w, w.fc_b, m->ff, 4 * E, 4 * E, E, EPI_BIAS_GELU));
+        LAUNCH(mm(m->ff, 4 * E, w.mlp_w, w.mlp_b, m->x, E, E, 4 * E, EPI_BIAS_RESID));
+    }
+    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, B, E, eps, st));
+    if (small) {
+        LAUNCH(launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val, m->d_am_idx, st));
+        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, gemv_argmax_blocks(V), B, m->d_next, st));
+    } else {
+        LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, B, V, E, EPI_STORE, st));
+        LAUNCH(launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st));
+    }
+    if (advance) LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
+    return MODEL_OK;
+}
+
+// Runs one decode step, from a graph when statistics are off.
+model_status decode_step(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
+    if (m->stats_on) return run_decode(m, B, cache, advance, out, ld_out);
+    const GraphKey key{B, cache, advance, out, ld_out};
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        CU(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+        const uint64_t before = m->launches;
+        model_status rc = run_decode(m, B, cache, advance, out, ld_out);
+        cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+        const uint64_t kernels = m->launches - before;
+        m->launches = before;  // counted when the graph runs
+        if (rc != MODEL_OK) { if (g) cudaGraphDestroy(g); return rc; }
+        if (ce != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; }
+        cudaGraphExec_t ex = nullptr;
+        ce = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; }
+        it = m->graphs.emplace(key, GraphEntry{ex, kernels}).first;
+    }
+    CU(cudaGraphLaunch(it->second.exec, m->st));
+    m->launches += it->second.kernels;
+    return MODEL_OK;
+}
+
+model_status copy_ids_to_device(model* m, const int32_t* ids, size_t n) {
+    model_status rc = ensure_rows(m, n);
+    if (rc != MODEL_OK) return rc;
+    CU(cudaMemcpyAsync(m->d_ids, ids, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    return MODEL_OK;
+}
+
+model_status set_slot_state(model* m, size_t B, const int32_t* tokens, const int32_t* lens) {
+    model_status rc = ensure_pinned(m, 2 * B);
+    if (rc != MODEL_OK) return rc;
+    CU(cudaStreamSynchronize(m->st));
+    std::memcpy(m->h_small, tokens, B * sizeof(int32_t));
+    std::memcpy(m->h_small + B, lens, B * sizeof(int32_t));
+    CU(cudaMemcpyAsync(m->d_tokens, m->h_small, B * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    CU(cudaMemcpyAsync(m->d_lens, m->h_small + B, B * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    return MODEL_OK;
+}
+
+model_status finish(model* m) {
+    CU(cudaStreamSynchronize(m->st));
+    return stats_end(m);
+}
+
+// --------------------------------------------------------------- loading --
+// The inventory record and the weight file header must agree with each other
+// and with the config (model.c:287-317); nothing is read here.
+model_status check_tensor(st_file* f, const std::string& inv, const char* name, int nd, long long d0,
+                          long long d1, InvEntry* out, const st_tensor** out_t) {
+    InvEntry e;
+    if (!inventory_find(inv, name, &e)) return MODEL_ERR_INVENTORY;
+    if (std::strcmp(e.dtype, "F32") != 0) return MODEL_ERR_DTYPE;
+    if (e.n_dims != nd || e.dims[0] != d0 || (nd == 2 && e.dims[1] != d1)) return MODEL_ERR_SHAPE;
+    const st_tensor* t = nullptr;
+    if (st_find(f, name, &t) != ST_OK) return MODEL_ERR_INVENTORY;
+    if (t->dtype != ST_DTYPE_F32) return MODEL_ERR_DTYPE;
+    if (t->n_dims != nd) return MODEL_ERR_INVENTORY;
+    for (int i = 0; i < nd; ++i) if (t->dims[i] != e.dims[i]) return MODEL_ERR_INVENTORY;
+    if (t->nbytes != e.nbytes || t->file_offset != e.file_offset) return MODEL_ERR_INVENTORY;
+    const size_t n = (size_t)d0 * (size_t)(nd == 2 ? d1 : 1);
+    if (t->nbytes != n * sizeof(float)) return MODEL_ERR_SHAPE;
+    if (out) *out = e;
+    if (out_t) *out_t = t;
+    return MODEL_OK;
+}
+
+model_status load_tensor(model* m, st_file* f, const std::string& inv, const char* name, int nd,
+                         long long d0, long long d1, std::vector<float>* host, InvEntry* out) {
+    (void)m;
+    const st_tensor* t = nullptr;
+    model_status rc = check_tensor(f, inv, name, nd, d0, d1, out, &t);
+    if (rc != MODEL_OK) return rc;
+    try { host->resize((size_t)(t->nbytes / sizeof(float))); } catch (...) { return MODEL_ERR_NOMEM; }
+    if (st_tensor_read(f, t, host->data(), t->nbytes) != ST_OK) return MODEL_ERR_WEIGHTS;
+    return MODEL_OK;
+}
+
+// Every tensor the forward pass uses, checked before any device work so that a
+// bad artifact is refused without touching the GPU.
+model_status check_all(st_file* f, const std::string& inv, const model_config& c) {
+    const long long E = c.n_embd;
+    struct Want { std::string name; int nd; long long d0, d1; };
+    std::vector<Want> w = {{"wte.weight", 2, c.vocab_size, E}, {"wpe.weight", 2, c.n_ctx, E},
+                           {"ln_f.weight", 1, E, 0}, {"ln_f.bias", 1, E, 0}};
+    for (int l = 0; l < c.n_layer; ++l) {
+        const std::string p = "h." + std::to_string(l) + ".";
+        w.push_back({p + "ln_1.weight", 1, E, 0});
+        w.push_back({p + "ln_1.bias", 1, E, 0});
+        w.push_back({p + "attn.c_attn.weight", 2, E, 3 * E});
+        w.push_back({p + "attn.c_attn.bias", 1, 3 * E, 0});
+        w.push_back({p + "attn.c_proj.weight", 2, E, E});
+        w.push_back({p + "attn.c_proj.bias", 1, E, 0});
+        w.push_back({p + "ln_2.weight", 1, E, 0});
+        w.push_back({p + "ln_2.bias", 1, E, 0});
+        w.push_back({p + "mlp.c_fc.weight", 2, E, 4 * E});
+        w.push_back({p + "mlp.c_fc.bias", 1, 4 * E, 0});
+        w.push_back({p + "mlp.c_proj.weight", 2, 4 * E, E});
+        w.push_back({p + "mlp.c_proj.bias", 1, E, 0});
+    }
+    for (const Want& x : w) {
+        model_status rc = check_tensor(f, inv, x.name.c_str(), x.nd, x.d0, x.d1, nullptr, nullptr);
+        if (rc != MODEL_OK) return rc;
+    }
+    return MODEL_OK;
+}
+
+void record(model* m, const char* name, const InvEntry& e, int transposed, const char* how) {
+    model_tensor_record r;
+    std::memset(&r, 0, sizeof r);
+    std::snprintf(r.name, sizeof r.name, "%s", name);
+    if (e.n_dims == 2) std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lldx%lld", e.dims[0], e.dims[1]);
+    else std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lld", e.dims[0]);
+    std::snprintf(r.inventory_orientation, sizeof r.inventory_orientation, "%s", e.orientation);
+    r.transposed_at_load = transposed;
+    std::snprintf(r.reconciliation, sizeof r.reconciliation, "%s", how);
+    m->records.push_back(r);
+}
+
+model_status load_impl(const char* weights_path, const char* inventory_path, const char* config_path,
+                       model_cproj_reading cproj, int device, model** out) {
+    if (!weights_path || !inventory_path || !config_path || !out) return MODEL_ERR_ARG;
+    *out = nullptr;
+    std::string cfg_text, inv;
+    if (!read_text(config_path, &cfg_text)) return MODEL_ERR_OPEN;
+    if (!read_text(inventory_path, &inv)) return MODEL_ERR_OPEN;
+
+    model* m = new (std::nothrow) model();
+    if (!m) return MODEL_ERR_NOMEM;
+    m->cproj = cproj;
+    model_status rc = MODEL_OK;
+    st_file* f = nullptr;
+    std::vector<float> host, tmp_host;
+    float* staging = nullptr;
+    const char* c = cfg_text.c_str();
+    double eps = 0.0;
+    model_config& cf = m->cfg;
+    if (!json_int(c, "n_layer", &cf.n_layer) || !json_int(c, "n_head", &cf.n_head) ||
+        !json_int(c, "n_embd", &cf.n_embd) || !json_int(c, "n_ctx", &cf.n_ctx) ||
+        !json_int(c, "vocab_size", &cf.vocab_size) || !json_num(c, "layer_norm_epsilon", &eps) ||
+        !json_str(c, "activation_function", cf.activation_function, sizeof cf.activation_function)) {
+        rc = MODEL_ERR_CONFIG;
+        goto fail;
+    }
+    cf.layer_norm_epsilon = (float)eps;
+    if (cf.n_head <= 0 || cf.n_embd % cf.n_head != 0) { rc = MODEL_ERR_CONFIG; goto fail; }
+    cf.head_dim = cf.n_embd / cf.n_head;
+    if (std::strcmp(cf.activation_function, "gelu_new") != 0) { rc = MODEL_ERR_CONFIG; goto fail; }
+    // The kernels are written for GPT-2's head width and 16-byte rows.
+    if (cf.head_dim != 64 || cf.n_embd % 4 != 0 || cf.n_layer <= 0 || cf.n_ctx <= 0 ||
+        cf.vocab_size <= 0) {
+        rc = MODEL_ERR_CONFIG;
+        goto fail;
+    }
+    {
+        const char* cv = std::strstr(inv.c_str(), "\"config_values_used\"");
+        int ie = 0, il = 0, ih = 0, iv = 0;
+        if (!cv || !json_int(cv, "n_embd", &ie) || !json_int(cv, "n_layer", &il) ||
+            !json_int(cv, "n_head", &ih) || !json_int(cv, "vocab_size", &iv)) {
+            rc = MODEL_ERR_INVENTORY;
+            goto fail;
+        }
+        if (ie != cf.n_embd || il != cf.n_layer || ih != cf.n_head || iv != cf.vocab_size) {
+            rc = MODEL_ERR_INVENTORY;
+            goto fail;
+        }
+    }
+    if (st_open(weights_path, &f) != ST_OK) { rc = MODEL_ERR_WEIGHTS; goto fail; }
+    if ((rc = check_all(f, inv, cf)) != MODEL_OK) goto fail;
+
+    {
+        if (cudaSetDevice(device) != cudaSuccess) { cudaGetLastError(); rc = MODEL_ERR_DEVICE; goto fail; }
+        m->device = device;
+        if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            rc = MODEL_ERR_DEVICE;
+            goto fail;
+        }
+        const size_t E = (size_t)cf.n_embd, V = (size_t)cf.vocab_size, L = (size_t)cf.n_layer;
+        const size_t per_layer = 4 * E + 3 * E * E + 3 * E + E * E + E + 4 * E * E + 4 * E + 4 * E * E + E;
+        const size_t total = V * E + (size_t)cf.n_ctx * E + 2 * E + L * per_layer;
+        m->weight_bytes = total * sizeof(float);
+        if (cudaMalloc(&m->d_weights, m->weight_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            rc = MODEL_ERR_NOMEM;
+            goto fail;
+        }
+        if (cudaMalloc(&staging, 4 * E * E * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            rc = MODEL_ERR_NOMEM;
+            goto fail;
+        }
+        float* cursor = m->d_weights;
+        auto take = [&](size_t n) { float* p = cursor; cursor += n; return p; };
+        // uploads `host` (d0 x d1 row-major) to dst, transposed to d1 x d0 when asked
+        auto upload = [&](float* dst, size_t d0, size_t d1, bool transpose) -> model_status {
+            if (!transpose) {
+                CU(cudaMemcpy(dst, host.data(), d0 * d1 * sizeof(float), cudaMemcpyHostToDevice));
+            } else {
+                CU(cudaMemcpy(staging, host.data(), d0 * d1 * sizeof(float), cudaMemcpyHostToDevice));
+                CU(launch_transpose(staging, dst, (int)d0, (int)d1, nullptr));
+                CU(cudaDeviceSynchronize());
+            }
+            return MODEL_OK;
+        };
+        InvEntry e;
+#define TRY(x) do { rc = (x); if (rc != MODEL_OK) goto fail; } while (0)
+        TRY(load_tensor(m, f, inv, "wte.weight", 2, cf.vocab_size, cf.n_embd, &host, &e));
+        m->wte = take(V * E);
+        TRY(upload(m->wte, V, E, false));
+        record(m, "wte.weight", e, 0, "rows are tokens: the lookup table and, as stored, the tied head");
+        TRY(load_tensor(m, f, inv, "wpe.weight", 2, cf.n_ctx, cf.n_embd, &host, &e));
+        m->wpe = take((size_t)cf.n_ctx * E);
+        TRY(upload(m->wpe, cf.n_ctx, E, false));
+        record(m, "wpe.weight", e, 0, "rows are positions: learned absolute, as stored");
+        TRY(load_tensor(m, f, inv, "ln_f.weight", 1, cf.n_embd, 0, &host, &e));
+        m->lnf_w = take(E);
+        TRY(upload(m->lnf_w, 1, E, false));
+        TRY(load_tensor(m, f, inv, "ln_f.bias", 1, cf.n_embd, 0, &host, &e));
+        m->lnf_b = take(E);
+        TRY(upload(m->lnf_b, 1, E, false));
+        m->layers.resize(L);
+        for (int l = 0; l < cf.n_layer; ++l) {
+            Layer& y = m->layers[l];
+            char name[64];
+            auto vec = [&](const char* fmt, size_t n, float** dst) -> model_status {
+                std::snprintf(name, sizeof name, fmt, l);
+                model_status r = load_tensor(m, f, inv, name, 1, (long long)n, 0, &host, nullptr);
+                if (r != MODEL_OK) return r;
+                *dst = take(n);
+                return upload(*dst, 1, n, false);
+            };
+            // A matrix stored [in, out] in the file becomes [out, in] (K-major) on the
+            // device: the layout of every matmul kernel here.
+            auto mat = [&](const char* fmt, size_t din, size_t dout, bool stored_in_out,
+                           float** dst) -> model_status {
+                std::snprintf(name, sizeof name, fmt, l);
+                model_status r = load_tensor(m, f, inv, name, 2, (long long)din, (long long)dout, &host, &e);
+                if (r != MODEL_OK) return r;
+                *dst = take(din * dout);
+                return upload(*dst, din, dout, stored_in_out);
+            };
+            TRY(vec("h.%d.ln_1.weight", E, &y.ln1_w));
+            TRY(vec("h.%d.ln_1.bias", E, &y.ln1_b));
+            TRY(mat("h.%d.attn.c_attn.weight", E, 3 * E, true, &y.qkv_w));
+            if (l == 0) record(m, "h.*.attn.c_attn.weight", e, 0,
+                               "[input, output] as stored; held [output, input] on the device");
+            TRY(vec("h.%d.attn.c_attn.bias", 3 * E, &y.qkv_b));
+            // c_proj: the AS_STORED reading is [input, output]; the TRANSPOSED
+            // reading takes the file as [output, input] (model.c:435).
+            TRY(mat("h.%d.attn.c_proj.weight", E, E, cproj == MODEL_CPROJ_AS_STORED, &y.proj_w));
+            if (l == 0) record(m, "h.*.attn.c_proj.weight", e, cproj == MODEL_CPROJ_TRANSPOSED,
+                               cproj == MODEL_CPROJ_TRANSPOSED
+                                   ? "unresolved by shape; TRANSPOSED reading, i.e. stored [output, input]"
+                                   : "unresolved by shape; AS STORED reading, i.e. [input, output]");
+            TRY(vec("h.%d.attn.c_proj.bias", E, &y.proj_b));
+            TRY(vec("h.%d.ln_2.weight", E, &y.ln2_w));
+            TRY(vec("h.%d.ln_2.bias", E, &y.ln2_b));
+            TRY(mat("h.%d.mlp.c_fc.weight", E, 4 * E, true, &y.fc_w));
+            if (l == 0) record(m, "h.*.mlp.c_fc.weight", e, 0,
+                               "[input, output] as stored; held [output, input] on the device");
+            TRY(vec("h.%d.mlp.c_fc.bias", 4 * E, &y.fc_b));
+            TRY(mat("h.%d.mlp.c_proj.weight", 4 * E, E, true, &y.mlp_w));
+            if (l == 0) record(m, "h.*.mlp.c_proj.weight", e, 0,
+                               "[input, output] as stored; held [output, input] on the device");
+            TRY(vec("h.%d.mlp.c_proj.bias", E, &y.mlp_b));
+        }
+#undef TRY
+    }
+    cudaFree(staging);
+    st_close(f);
+    *out = m;
+    return MODEL_OK;
+fail:
+    cudaFree(staging);
+    if (f) st_close(f);
+    model_free(m);
+    return rc;
+}
+
+}  // namespace
+
+// ================================================================== the ABI ==
+extern "C" {
+
+const char* model_strerror(model_status s) {
+    switch (s) {
+        case MODEL_OK: return "ok";
+        case MODEL_ERR_OPEN: return "an artifact could not be opened";
+        case MODEL_ERR_CONFIG: return "config.json is missing a field or names an unsupported architecture";
+        case MODEL_ERR_INVENTORY: return "the inventory disagrees with the weight file";
+        case MODEL_ERR_WEIGHTS: return "the weight file failed to open, parse or read";
+        case MODEL_ERR_SHAPE: return "a tensor's shape contradicts the config";
+        case MODEL_ERR_DTYPE: return "a tensor is not F32";
+        case MODEL_ERR_RANGE: return "a token id or position is out of range";
+        case MODEL_ERR_CAPACITY: return "a caller-owned buffer or the cache is too small";
+        case MODEL_ERR_NOMEM: return "allocation failed";
+        case MODEL_ERR_ARG: return "a null or unusable argument";
+        case MODEL_ERR_DEVICE: return "a CUDA call failed";
+    }
+    return "unknown";
+}
+
+model_status model_load(const char* weights_path, const char* inventory_path, const char* config_path,
+                        model_cproj_reading cproj_reading, model** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); dev = 0; }
+    return load_impl(weights_path, inventory_path, config_path, cproj_reading, dev, out);
+}
+
+model_status model_load_on_device(const char* weights_path, const char* inventory_path,
+                                  const char* config_path, model_cproj_reading cproj_reading,
+                                  int device, model** out) {
+    return load_impl(weights_path, inventory_path, config_path, cproj_reading, device, out);
+}
+
+void model_free(model* m) {
+    if (!m) return;
+    if (m->st) cudaStreamSynchronize(m->st);
+    drop_graphs(m);
+    cudaFree(m->d_weights);
+    cudaFree(m->x); cudaFree(m->xb); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->ff);
+    cudaFree(m->logits); cudaFree(m->d_ids);
+    cudaFree(m->d_tokens); cudaFree(m->d_lens); cudaFree(m->d_next); cudaFree(m->d_step);
+    cudaFree(m->d_out); cudaFree(m->d_part); cudaFree(m->d_am_val); cudaFree(m->d_am_idx);
+    cudaFree(m->d_stats);
+    if (m->h_small) cudaFreeHost(m->h_small);
+    kv_cache_destroy(m->kv);
+    kv_cache_destroy(m->pool);
+    if (m->st) cudaStreamDestroy(m->st);
+    cudaGetLastError();
+    delete m;
+}
+
+const model_config* model_config_of(const model* m) { return m ? &m->cfg : nullptr; }
+model_cproj_reading model_cproj_reading_of(const model* m) { return m ? m->cproj : MODEL_CPROJ_AS_STORED; }
+size_t model_tensor_record_count(const model* m) { return m ? m->records.size() : 0; }
+const model_tensor_record* model_tensor_record_at(const model* m, size_t i) {
+    return (m && i < m->records.size()) ? &m->records[i] : nullptr;
+}
+
+// The forward pass has no substitutable CPU matmul; the choice is recorded and
+// the engine's own kernels keep running (model_gemm_of reports them).
+void model_set_gemm(model* m, const gemm_impl* impl) { if (m && impl) m->gemm_choice = impl; }
+const gemm_impl* model_gemm_of(const model* m) { return m ? &gemm_impl_sm100a : nullptr; }
+
+void model_set_decode_path(model* m, model_decode_path p) {
+    if (m && (p == MODEL_PATH_NOCACHE || p == MODEL_PATH_CACHE)) m->path = p;
+}
+model_decode_path model_decode_path_of(const model* m) { return m ? m->path : MODEL_PATH_NOCACHE; }
+
+model_status model_reserve(model* m, size_t T) {
+    if (!m) return MODEL_ERR_ARG;
+    if (T == 0) T = 1;
+    model_status rc = ensure_rows(m, T);
+    if (rc != MODEL_OK) return rc;
+    rc = ensure_logits(m, T);
+    if (rc != MODEL_OK) return rc;
+    return ensure_slots(m, 1, m->cfg.n_ctx);
+}
+
+model_status model_kv_reserve(model* m, size_t capacity) {
+    if (!m) return MODEL_ERR_ARG;
+    if (capacity == 0) return MODEL_ERR_ARG;
+    if ((int)capacity > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    if (m->kv && kv_cache_capacity(m->kv) >= (int)capacity) return MODEL_OK;
+    kv_cache* fresh = nullptr;
+    kv_status ks = kv_cache_create(m->cfg.n_layer, m->cfg.n_embd, (int)capacity, &fresh);
+    if (ks == KV_ERR_NOMEM) return MODEL_ERR_NOMEM;
+    if (ks != KV_OK) return MODEL_ERR_ARG;
+    drop_graphs(m);
+    kv_cache_destroy(m->kv);
+    m->kv = fresh;
+    return MODEL_OK;
+}
+
+size_t model_kv_footprint_bytes(const model* m) { return m ? kv_cache_footprint_bytes(m->kv) : 0u; }
+int model_kv_capacity(const model* m) { return m ? kv_cache_capacity(m->kv) : 0; }
+int model_kv_length(const model* m) { return m ? kv_cache_length(m->kv) : 0; }
+const kv_cache* model_kv_cache_of(const model* m) { return m ? m->kv : nullptr; }
+
+model_status model_kv_set_length(model* m, int length) {
+    if (!m || !m->kv) return MODEL_ERR_ARG;
+    kv_status ks = kv_cache_set_length(m->kv, length);
+    if (ks == KV_ERR_CAPACITY) return MODEL_ERR_CAPACITY;
+    return ks == KV_OK ? MODEL_OK : MODEL_ERR_ARG;
+}
+
+const float* model_token_embedding(const model* m) { return m ? m->wte : nullptr; }
+const float* model_head_weight(const model* m) { return m ? m->wte : nullptr; }
+
+void model_collect_attn_stats(model* m, int enable) {
+    if (!m) return;
+    m->stats_on = enable != 0;
+    m->rs_min = m->rs_max = 0.0;
+    m->rs_rows = 0;
+}
+
+void model_attn_rowsum_range(const model* m, double* lo, double* hi, size_t* rows) {
+    if (lo) *lo = m ? m->rs_min : 0.0;
+    if (hi) *hi = m ? m->rs_max : 0.0;
+    if (rows) *rows = m ? m->rs_rows : 0;
+}
+
+// model.c:920-925: a strict '>' scan of a HOST buffer; lowest index wins ties.
+int32_t model_argmax(const float* v, size_t n) {
+    int32_t best = 0;
+    for (size_t i = 1; i < n; ++i) if (v[i] > v[best]) best = (int32_t)i;
+    return best;
+}
+
+// model.c:593-603, computed by the engine's LayerNorm kernel with unit gain and
+// zero shift (x * 1 + 0 leaves the normalised value unchanged). Host arrays in
+// and out; NaN is written if no device is usable.
+void model_layernorm_normalize(const float* x, int n, float eps, float* out) {
+    if (!x || !out || n <= 0) return;
+    float* d = nullptr;
+    std::vector<float> ones((size_t)n, 1.0f);
+    bool ok = cudaMalloc(&d, (size_t)n * 4 * 4) == cudaSuccess;
+    if (ok) {
+        float *dx = d, *dy = d + n, *dg = d + 2 * (size_t)n, *db = d + 3 * (size_t)n;
+        ok = cudaMemcpy(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(dg, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemset(db, 0, (size_t)n * 4) == cudaSuccess &&
+             launch_layernorm(dx, dg, db, dy, 1, n, eps, nullptr) == cudaSuccess &&
+             cudaMemcpy(out, dy, (size_t)n * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    cudaFree(d);
+    if (!ok) {
+        cudaGetLastError();
+        for (int i = 0; i < n; ++i) out[i] = NAN;
+    }
+}
+
+// ---------------------------------------------------------------- prefill --
+model_status model_prefill(model* m, const int32_t* ids, size_t T, float* logits, size_t cap) {
+    if (!m || !ids || !logits) return MODEL_ERR_ARG;
+    if (cap < T * (size_t)m->cfg.vocab_size) return MODEL_ERR_CAPACITY;
+    model_status rc = model_reserve(m, T);
+    if (rc != MODEL_OK) return rc;
+    // forward_blocks' refusals, all before any launch (model.c:660-668)
+    const bool use_cache = m->path == MODEL_PATH_CACHE;
+    if (T == 0) return MODEL_ERR_ARG;
+    if ((int)T > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    for (size_t t = 0; t < T; ++t)
+        if (ids[t] < 0 || ids[t] >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    if (use_cache) {
+        if (!m->kv) return MODEL_ERR_ARG;
+        if ((int)T > kv_cache_capacity(m->kv)) return MODEL_ERR_CAPACITY;
+    }
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    if ((rc = copy_ids_to_device(m, ids, T)) != MODEL_OK) return rc;
+    if ((rc = run_prefill(m, 1, (int)T, use_cache ? m->kv : nullptr, 0)) != MODEL_OK) return rc;
+    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    // the tied head at every position (model.c:778-780)
+    LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, (int)T, V, E, EPI_STORE, m->st));
+    CU(cudaMemcpyAsync(logits, m->logits, T * (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
+    if ((rc = finish(m)) != MODEL_OK) return rc;
+    if (use_cache) kv_cache_set_length(m->kv, (int)T);
+    return MODEL_OK;
+}
+
+// ----------------------------------------------------------------- decode --
+static model_status cached_step(model* m, const int32_t* ids, size_t T, float* logits, int32_t* next) {
+    model_status rc = model_reserve(m, T);
+    if (rc != MODEL_OK) return rc;
+    const int32_t id = ids[T - 1];
+    if (id < 0 || id >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    if ((rc = ensure_slots(m, 1, m->kv->capacity)) != MODEL_OK) return rc;
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    const int32_t len = (int32_t)(T - 1);
+    if ((rc = set_slot_state(m, 1, &id, &len)) != MODEL_OK) return rc;
+    if ((rc = decode_step(m, 1, m->kv, false, nullptr, 0)) != MODEL_OK) return rc;
+    if (logits)
+        CU(cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab_size * sizeof(float),
+                           cudaMemcpyDeviceToHost, m->st));
+    if (next) CU(cudaMemcpyAsync(m->h_small, m->d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    if ((rc = finish(m)) != MODEL_OK) return rc;
+    if (next) *next = m->h_small[0];
+    kv_cache_set_length(m->kv, (int)T);
+    return MODEL_OK;
+}
+
+model_status model_decode_step_cached(model* m, const int32_t* ids, size_t T, float* logits, size_t cap) {
+    if (!m || !ids || !logits) return MODEL_ERR_ARG;
+    if (cap < (size_t)m->cfg.vocab_size) return MODEL_ERR_CAPACITY;
+    if (T == 0) return MODEL_ERR_ARG;
+    if ((int)T > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    if (!m->kv) return MODEL_ERR_ARG;
+    if ((int)T > kv_cache_capacity(m->kv)) return MODEL_ERR_CAPACITY;
+    if (kv_cache_length(m->kv) != (int)(T - 1)) return MODEL_ERR_ARG;
+    return cached_step(m, ids, T, logits, nullptr);
+}
+
+model_status model_decode_step_greedy(model* m, const int32_t* ids, size_t T, int32_t* next) {
+    if (!m || !ids || !next) return MODEL_ERR_ARG;
+    if (T == 0) return MODEL_ERR_ARG;
+    if ((int)T > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    if (!m->kv) return MODEL_ERR_ARG;
+    if ((int)T > kv_cache_capacity(m->kv)) return MODEL_ERR_CAPACITY;
+    if (kv_cache_length(m->kv) != (int)(T - 1)) return MODEL_ERR_ARG;
+    return cached_step(m, ids, T, nullptr, next);
+}
+
+model_status model_decode_step(model* m, const int32_t* ids, size_t T, float* logits, size_t cap) {
+    if (!m || !ids || !logits) return MODEL_ERR_ARG;
+    if (m->path == MODEL_PATH_CACHE) return model_decode_step_cached(m, ids, T, logits, cap);
+    if (cap < (size_t)m->cfg.vocab_size) return MODEL_ERR_CAPACITY;
+    model_status rc = model_reserve(m, T);
+    if (rc != MODEL_OK) return rc;
+    if (T == 0) return MODEL_ERR_ARG;
+    if ((int)T > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    for (size_t t = 0; t < T; ++t)
+        if (ids[t] < 0 || ids[t] >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    if ((rc = copy_ids_to_device(m, ids, T)) != MODEL_OK) return rc;
+    if ((rc = run_prefill(m, 1, (int)T, nullptr, 0)) != MODEL_OK) return rc;
+    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    // the head at the last position only, with prefill's kernel (model.c:913-916)
+    LAUNCH(launch_gemm_tn(m->xb + (T - 1) * (size_t)E, E, m->wte, E, nullptr, m->logits, V, 1, V, E,
+                          EPI_STORE, m->st));
+    CU(cudaMemcpyAsync(logits, m->logits, (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
+    return finish(m);
+}
+
+// ----------------------------------------------------------------- batches --
+int model_device(const model* m) { return m ? m->device : -1; }
+void* model_stream(const model* m) { return m ? (void*)m->st : nullptr; }
+size_t model_weight_device_bytes(const model* m) { return m ? m->weight_bytes : 0; }
+uint64_t model_kernel_launches(const model* m) { return m ? m->launches : 0; }
+
+model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
+    if (!m || n_seq == 0 || capacity == 0) return MODEL_ERR_ARG;
+    if ((int)capacity > m->cfg.n_ctx) return MODEL_ERR_RANGE;
+    if (n_seq > 1024) return MODEL_ERR_ARG;
+    if (!m->pool || m->pool->n_seq < (int)n_seq || m->pool->capacity < (int)capacity) {
+        kv_cache* fresh = nullptr;
+        kv_status ks = kv_pool_create(m->cfg.n_layer, m->cfg.n_embd, (int)n_seq, (int)capacity, &fresh);
+        if (ks != KV_OK) return ks == KV_ERR_NOMEM ? MODEL_ERR_NOMEM : MODEL_ERR_ARG;
+        drop_graphs(m);
+        kv_cache_destroy(m->pool);
+        m->pool = fresh;
+    }
+    model_status rc = ensure_rows(m, n_seq * capacity);
+    if (rc != MODEL_OK) return rc;
+    rc = ensure_slots(m, n_seq, m->pool->capacity);
+    if (rc != MODEL_OK) return rc;
+    return ensure_logits(m, n_seq);
+}
+
+static model_status batch_prefill_impl(model* m, size_t n_seq, size_t T, float* logits_host,
+                                       int32_t* next_host, bool host_ids, const int32_t* ids) {
+    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    model_status rc;
+    if (host_ids) {
+        if ((rc = copy_ids_to_device(m, ids, n_seq * T)) != MODEL_OK) return rc;
+    } else {
+        CU(cudaMemcpyAsync(m->d_ids, ids, n_seq * T * sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st));
+    }
+    if ((rc = run_prefill(m, (int)n_seq, (int)T, m->pool, 0)) != MODEL_OK) return rc;
+    if (logits_host) {
+        if ((rc = ensure_logits(m, n_seq * T)) != MODEL_OK) return rc;
+        LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, (int)(n_seq * T), V, E, EPI_STORE, m->st));
+        CU(cudaMemcpyAsync(logits_host, m->logits, n_seq * T * (size_t)V * sizeof(float),
+                           cudaMemcpyDeviceToHost, m->st));
+        LAUNCH(launch_argmax_rows(m->logits, V, (int)n_seq, V, (int)T, (int)T - 1, m->d_next, m->st));
+    } else {
+        // head only at each sequence's last position: rows (T-1) + s*T of xb
+        LAUNCH(launch_gemm_tn(m->xb + (T - 1) * (size_t)E, (int)(T * E), m->wte, E, nullptr, m->logits, V,
+                              (int)n_seq, V, E, EPI_STORE, m->st));
+        LAUNCH(launch_argmax_rows(m->logits, V, (int)n_seq, V, 1, 0, m->d_next, m->st));
+    }
+    (void)next_host;
+    return MODEL_OK;
+}
+
+model_status model_prefill_batch(model* m, const int32_t* ids, size_t n_seq, size_t T, float* logits,
+                                 size_t cap, int32_t* next_ids) {
+    if (!m || !ids || n_seq == 0 || T == 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)n_seq > m->pool->n_seq) return MODEL_ERR_ARG;
+    if ((int)T > m->pool->capacity) return MODEL_ERR_CAPACITY;
+    if (logits && cap < n_seq * T * (size_t)m->cfg.vocab_size) return MODEL_ERR_CAPACITY;
+    for (size_t i = 0; i < n_seq * T; ++i)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    model_status rc = ensure_rows(m, n_seq * T);
+    if (rc != MODEL_OK) return rc;
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    if ((rc = batch_prefill_impl(m, n_seq, T, logits, next_ids, true, ids)) != MODEL_OK) return rc;
+    if (next_ids)
+        CU(cudaMemcpyAsync(next_ids, m->d_next, n_seq * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    if ((rc = finish(m)) != MODEL_OK) return rc;
+    m->pool->length = (int)T;
+    return MODEL_OK;
+}
+
+model_status model_decode_step_batch(model* m, const int32_t* ids, size_t n_seq, float* logits,
+                                     size_t cap, int32_t* next_ids) {
+    if (!m || !ids || n_seq == 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)n_seq > m->pool->n_seq) return MODEL_ERR_ARG;
+    if (logits && cap < n_seq * (size_t)m->cfg.vocab_size) return MODEL_ERR_CAPACITY;
+    for (size_t i = 0; i < n_seq; ++i)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    if (m->pool->length + 1 > m->pool->capacity) return MODEL_ERR_CAPACITY;
+    model_status rc = ensure_slots(m, n_seq, m->pool->capacity);
+    if (rc != MODEL_OK) return rc;
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    std::vector<int32_t> lens(n_seq, (int32_t)m->pool->length);
+    if ((rc = set_slot_state(m, n_seq, ids, lens.data())) != MODEL_OK) return rc;
+    if ((rc = decode_step(m, (int)n_seq, m->pool, false, nullptr, 0)) != MODEL_OK) return rc;
+    if (logits)
+        CU(cudaMemcpyAsync(logits, m->logits, n_seq * (size_t)m->cfg.vocab_size * sizeof(float),
+                           cudaMemcpyDeviceToHost, m->st));
+    if (next_ids)
+        CU(cudaMemcpyAsync(next_ids, m->d_next, n_seq * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    if ((rc = finish(m)) != MODEL_OK) return rc;
+    m->pool->length += 1;
+    return MODEL_OK;
+}
+
+static model_status generate_impl(model* m, const int32_t* prompts, size_t n_seq, size_t T, size_t n_new,
+                                  int32_t* out_ids, bool host) {
+    if (!m || !prompts || !out_ids || n_seq == 0 || T == 0 || n_new == 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)n_seq > m->pool->n_seq) return MODEL_ERR_ARG;
+    if (T + n_new - 1 > (size_t)m->pool->capacity) return MODEL_ERR_CAPACITY;
+    if (host)
+        for (size_t i = 0; i < n_seq * T; ++i)
+            if (prompts[i] < 0 || prompts[i] >= m->cfg.vocab_size) return MODEL_ERR_RANGE;
+    model_status rc = ensure_rows(m, n_seq * T);
+    if (rc != MODEL_OK) return rc;
+    if ((rc = ensure_slots(m, n_seq, m->pool->capacity)) != MODEL_OK) return rc;
+    int32_t* d_out = out_ids;
+    if (host) {
+        size_t cap = m->out_cap;
+        if ((rc = grow(&m->d_out, &cap, n_seq * n_new)) != MODEL_OK) return rc;
+        m->out_cap = cap;
+        d_out = m->d_out;
+    }
+    if ((rc = stats_begin(m)) != MODEL_OK) return rc;
+    if ((rc = batch_prefill_impl(m, n_seq, T, nullptr, nullptr, host, prompts)) != MODEL_OK) return rc;
+    // The prefill's greedy choice is new token 0. One step_advance records it,
+    // makes it the next input and moves every length from T - 1 to T; each
+    // decode-step graph then ends with the same advance.
+    if ((rc = ensure_pinned(m, n_seq)) != MODEL_OK) return rc;
+    CU(cudaStreamSynchronize(m->st));
+    for (size_t i = 0; i < n_seq; ++i) m->h_small[i] = (int32_t)T - 1;
+    CU(cudaMemcpyAsync(m->d_lens, m->h_small, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+    CU(cudaMemsetAsync(m->d_step, 0, sizeof(int32_t), m->st));
+    LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, d_out, (int)n_new, m->d_step, (int)n_seq, m->st));
+    for (size_t g = 1; g < n_new; ++g)
+        if ((rc = decode_step(m, (int)n_seq, m->pool, true, d_out, (int)n_new)) != MODEL_OK) return rc;
+    if (host)
+        CU(cudaMemcpyAsync(out_ids, d_out, n_seq * n_new * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
+    m->pool->length = (int)(T + n_new - 1);
+    if (host) return finish(m);
+    return MODEL_OK;
+}
+
+model_status model_generate_greedy(model* m, const int32_t* prompts, size_t n_seq, size_t n_prompt,
+                                   size_t n_new, int32_t* out_ids) {
+    return generate_impl(m, prompts, n_seq, n_prompt, n_new, out_ids, true);
+}
+
+model_status model_generate_greedy_device(model* m, const int32_t* d_prompts, size_t n_seq,
+                                          size_t n_prompt, size_t n_new, int32_t* d_out_ids) {
+    return generate_impl(m, d_prompts, n_seq, n_prompt, n_new, d_out_ids, false);
+}
+
+model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context, int iters,
+                               float* avg_ms) {
+    if (!m || !avg_ms || rows == 0 || context == 0 || iters <= 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)rows > m->pool->n_seq || (int)context > m->pool->capacity) return MODEL_ERR_CAPACITY;
+    const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size, B = (int)rows;
+    const bool small = B <= 16;
+    cudaStream_t st = m->st;
+    model_status rc = ensure_slots(m, rows, m->pool->capacity);
+    if (rc != MODEL_OK) return rc;
+    if (kernel == TIE_KERNEL_PREFILL_ATTENTION || kernel == TIE_KERNEL_PREFILL_FC)
+        if ((rc = ensure_rows(m, rows * context)) != MODEL_OK) return rc;
+    // deterministic, finite contents for every operand
+    std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
+    if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    const size_t R = kernel >= TIE_KERNEL_PREFILL_ATTENTION ? rows * context : rows;
+    CU(cudaMemsetAsync(m->qkv, 0, R * 3 * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->xb, 0, R * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->ff, 0, R * 4 * E * sizeof(float), st));
+    const Layer& w = m->layers[0];
+    const PagedKV view = layer_view(m->pool, 0);
+    const int splits = attn_decode_max_splits(m->pool->capacity);
+    auto once = [&]() -> cudaError_t {
+        auto mm = [&](const float* X, int ldx, const float* Wt, const float* bias, float* Y, int ldy, int N,
+                      int K, int epi) {
+            return small ? launch_gemv(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st)
+                         : launch_gemm_tn(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st);
+        };
+        switch (kernel) {
+            case TIE_KERNEL_DECODE_ATTENTION:
+                return launch_attn_decode(m->qkv, m->d_lens, B, H, view, splits, m->d_part, m->attn, nullptr, st);
+            case TIE_KERNEL_DECODE_QKV: return mm(m->xb, E, w.qkv_w, w.qkv_b, m->qkv, 3 * E, 3 * E, E, EPI_BIAS);
+            case TIE_KERNEL_DECODE_FC: return mm(m->xb, E, w.fc_w, w.fc_b, m->ff, 4 * E, 4 * E, E, EPI_BIAS_GELU);
+            case TIE_KERNEL_DECODE_MLP_PROJ:
+                return mm(m->ff, 4 * E, w.mlp_w, w.mlp_b, m->x, E, E, 4 * E, EPI_BIAS_RESID);
+            case TIE_KERNEL_DECODE_HEAD:
+                if (small) {
+                    cudaError_t e = launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val,
+                                                       m->d_am_idx, st);
+                    return e != cudaSuccess ? e
+                                            : launch_argmax_finalize(m->d_am_val, m->d_am_idx,
+                                                                     gemv_argmax_blocks(V), B, m->d_next, st);
+                } else {
+                    cudaError_t e = launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, B, V, E, EPI_STORE, st);
+                    return e != cudaSuccess ? e : launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st);
+                }
+            case TIE_KERNEL_PREFILL_ATTENTION:
+                return launch_attn_prefill(m->qkv, B, (int)context, H, m->attn, nullptr, st);
+            case TIE_KERNEL_PREFILL_FC:
+                return launch_gemm_tn(m->xb, E, w.fc_w, E, w.fc_b, m->ff, 4 * E, (int)R, 4 * E, E, EPI_BIAS_GELU, st);
+        }
+        return cudaErrorInvalidValue;
+    };
+    CU(once());  // warm
+    cudaEvent_t a, b;
+    CU(cudaEventCreate(&a));
+    CU(cudaEventCreate(&b));
+    CU(cudaEventRecord(a, st));
+    for (int i = 0; i < iters; ++i) CU(once());
+    CU(cudaEventRecord(b, st));
+    CU(cudaEventSynchronize(b));
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    *avg_ms = ms / (float)iters;
+    return MODEL_OK;
+}
+
+}  // extern "C"
