@@ -60,6 +60,12 @@ def parse():
     p.add_argument("--workload", default="throughput", choices=sorted(WORKLOADS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernel", default=None,
+                   help="time one kernel alone (model_time_kernel) instead of the workload; "
+                        "used for profiler captures on a small case")
+    p.add_argument("--rows", type=int, default=128)
+    p.add_argument("--context", type=int, default=256)
+    p.add_argument("--iters", type=int, default=3)
     return p.parse_args()
 
 
@@ -399,9 +405,24 @@ def run_ours(args, rank, local_rank, world):
     return 0
 
 
+def run_kernel(args):
+    """One kernel of the GPT-2 small forward pass, alone, at (rows, context)."""
+    import tie_b200
+    w, inv, cfg = synth.ensure_model("small", seed=WEIGHT_SEED)
+    m = tie_b200.Model(w, inv, cfg, device=0)
+    m.batch_reserve(args.rows, args.context)
+    ms = m.time_kernel(args.kernel, args.rows, args.context, iters=args.iters)
+    print(json.dumps({"kernel": args.kernel, "rows": args.rows, "context": args.context,
+                      "iters": args.iters, "ms_per_launch": ms}), flush=True)
+    m.close()
+    return 0
+
+
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
+    if args.kernel:
+        return run_kernel(args)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
     return run_ours(args, rank, local_rank, world)
