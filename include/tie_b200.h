@@ -111,6 +111,31 @@ enum {
 model_status model_time_kernel(model *m, int kernel, size_t rows, size_t context, int iters,
                                float *avg_ms);
 
+/* ---- the greedy head without allocation --------------------------------
+ * No counterpart in the reference (its head is a CPU matmul over host memory).
+ * For callers that cannot allocate device memory -- a serving framework whose
+ * caching allocator already holds the GPU's memory, a plugin inside a runtime
+ * that forbids allocations outside its own allocator, a latency-bound loop that
+ * cannot take cudaMalloc's implicit device synchronisation.
+ *
+ * next[r] = argmax_j (x[r] . w[j]) for r < rows (lowest index on ties), and,
+ * when `logits` is non-NULL, logits[r * ldl + j] = x[r] . w[j]. x (rows x k,
+ * leading dimension ldx), w (vocab x k, ldw), logits and next are DEVICE
+ * pointers; x and w 16-byte aligned, k, ldx and ldw multiples of 4. Work is
+ * enqueued on `stream` (a cudaStream_t; NULL for the legacy default stream)
+ * and not waited for.
+ *
+ * Limits: rows <= 16 and vocab <= 65536, else MODEL_ERR_CAPACITY. The per-block
+ * partial maxima live in a fixed 512 KiB array inside the library, present on
+ * every GPU that loads it until the process exits; nothing is allocated per
+ * call. The array's device address is looked up on the first call made on each
+ * device (with that device current) -- make that first call before any stream
+ * capture. Every call shares the array, so calls that overlap on the GPU race
+ * on it. */
+model_status tie_head_argmax_noalloc(const float *x, int ldx, const float *w, int ldw, int rows,
+                                     int vocab, int k, float *logits, int ldl, int32_t *next,
+                                     void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -116,6 +116,8 @@ def library():
         "model_generate_greedy": (C.c_int, [_vp, _ip, C.c_size_t, C.c_size_t, C.c_size_t, _ip]),
         "model_generate_greedy_device": (C.c_int, [_vp, _vp, C.c_size_t, C.c_size_t, C.c_size_t, _vp]),
         "model_time_kernel": (C.c_int, [_vp, C.c_int, C.c_size_t, C.c_size_t, C.c_int, _fp]),
+        "tie_head_argmax_noalloc": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              _vp, C.c_int, _vp, _vp]),
         "kv_cache_footprint_for": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
         "kv_cache_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
         "kv_cache_destroy": (None, [_vp]),
