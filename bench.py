@@ -314,7 +314,9 @@ def run_ours(args, rank, local_rank, world):
     launches = (m.kernel_launches() - l0) // args.steps
     clocks = sampler.stop() if sampler else None
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
-    gen_tokens = wl["n_seq"] * n_new
+    # tokens a step produces: the generated ones, or for a prefill-only workload
+    # (one new token) the prompt tokens it processes
+    gen_tokens = wl["n_seq"] * (n_new if n_new > 1 else T)
     value = gen_tokens / (ms / 1e3)
 
     # the same generation through the public host API: pinned prompts in, ids out

@@ -64,10 +64,13 @@ void gemm_naive_bt(int M, int N, int K,
 /* reference src/gemm/gemm.h:89. name "gemm_naive_sm100a". */
 extern const gemm_impl gemm_impl_naive;
 
-/* Additive: the engine's own tiled sm_100a kernels behind the same two
- * signatures (fp32 operands, fp32 accumulate; tolerance-equal to the naive
- * order, not bit-equal). name "tie_b200_sm100a". This is what
- * model_gemm_of() reports. */
+/* Additive: the engine's own sm_100a kernels behind the same two signatures,
+ * name "tie_b200_sm100a" (what model_gemm_of() reports). mul_bt runs the
+ * tensor-core matmul (tcgen05, operands split into two tf32 halves, three MMAs
+ * per product, fp32 accumulate: relative error near 2^-21 per product) when K
+ * is a multiple of 32 and the leading dimensions of 4, else the tiled fp32
+ * FFMA kernel; mul runs the tiled fp32 FFMA kernel. Tolerance-equal to the
+ * naive order, not bit-equal. */
 extern const gemm_impl gemm_impl_sm100a;
 
 #ifdef __cplusplus

@@ -77,8 +77,11 @@ cudaError_t launch_embed_decode(const int32_t* tokens, const int32_t* lens, int 
                                 const float* wte, const float* wpe, float* x, int E, int V,
                                 cudaStream_t st);
 // y[r] = LN(x[r]) * g + b, statistics in double               (model.c:593-610)
+// y (fp32) and/or its tf32 split y_hi/y_lo (the tensor-core matmul's input);
+// either may be NULL.
 cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float* y, int rows,
-                             int E, float eps, cudaStream_t st);
+                             int E, float eps, cudaStream_t st, float* y_hi = nullptr,
+                             float* y_lo = nullptr);
 
 // C[M,N] (epilogue) = A[M,K] . W[N,K]^T, tiled fp32 SIMT GEMM (prefill)
 cudaError_t launch_gemm_tn(const float* A, int lda, const float* W, int ldw, const float* bias,
@@ -109,14 +112,18 @@ cudaError_t launch_kv_store_decode(const float* qkv, const int32_t* lens, int B,
 // Causal attention over T tokens per sequence from the fused qkv activations
 // (prefill, model.c:705-732): out[r, h*D:(h+1)*D].
 cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
-                                AttnStats* stats, cudaStream_t st);
+                                AttnStats* stats, cudaStream_t st, float* out_hi = nullptr,
+                                float* out_lo = nullptr);
 // One query per sequence against its cached positions 0..lens[b] (the new
 // position included), split over position chunks, then combined
 // (model.c:826-850).
 int attn_decode_max_splits(int capacity);
+// With `counters` (B * H ints, zero on first use; the kernel leaves them zero)
+// and no statistics, one fused kernel; else split + merge kernels.
 cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv,
                                int max_splits, float* part, float* out, AttnStats* stats,
-                               cudaStream_t st);
+                               cudaStream_t st, float* out_hi = nullptr, float* out_lo = nullptr,
+                               int* counters = nullptr);
 
 // Step bookkeeping for device-resident greedy generation: tokens[b] = next[b];
 // out[b * ld + *step] = next[b]; lens[b] += 1; (block 0 thread 0) *step += 1.

@@ -5,6 +5,7 @@
 // always a kernel. Calls are synchronous, like the reference's.
 #include "../../include/gemm.h"
 #include "internal.h"
+#include "tc_gemm.h"
 
 #include <cstdio>
 
@@ -55,6 +56,30 @@ void run(Kind kind, int M, int N, int K, const float* A, int lda, const float* B
         e = cudaErrorMemoryAllocation;
     } else if (kind == NAIVE_NN || kind == NAIVE_BT) {
         e = launch_gemm_naive(M, N, K, dA, lda, dB, ldb, dC, ldc, bt, nullptr);
+    } else if (kind == TILED_BT && K > 0 && tc_gemm_supported(M, N, K, lda, ldb)) {
+        // the tensor-core path: split both operands into tf32 halves, then 3xTF32
+        float* sp = nullptr;
+        const size_t na = span(M, K, lda), nb = span(N, K, ldb);  // what the kernel reads
+        e = cudaMalloc(&sp, 2 * (na + nb) * sizeof(float));
+        if (e == cudaSuccess) {
+            float *ah = sp, *al = sp + na, *bh = sp + 2 * na, *bl = bh + nb;
+            e = launch_split_hilo(dA, ah, al, (long long)na, nullptr);
+            if (e == cudaSuccess) e = launch_split_hilo(dB, bh, bl, (long long)nb, nullptr);
+            TcOperands op{ah, al, lda, bh, bl, ldb};
+            TcArgs a{};
+            a.M = M; a.N = N; a.K = K; a.C = dC; a.ldc = ldc;
+            int* err = nullptr;
+            if (e == cudaSuccess) e = cudaMalloc(&err, sizeof(int));
+            if (e == cudaSuccess) e = cudaMemset(err, 0, sizeof(int));
+            a.err = err;
+            if (e == cudaSuccess) e = launch_tc_gemm(op, a, EPI_STORE, TC_OUT_F32, 1, nullptr);
+            if (e == cudaSuccess) e = cudaDeviceSynchronize();
+            int flag = 0;
+            if (e == cudaSuccess) e = cudaMemcpy(&flag, err, sizeof flag, cudaMemcpyDeviceToHost);
+            if (e == cudaSuccess && flag) e = cudaErrorLaunchTimeout;
+            cudaFree(err);
+            cudaFree(sp);
+        }
     } else if (kind == TILED_BT) {
         e = launch_gemm_tn(dA, lda, dB, ldb, nullptr, dC, ldc, M, N, K, EPI_STORE, nullptr);
     } else {

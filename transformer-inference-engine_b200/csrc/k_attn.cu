@@ -8,13 +8,15 @@
 //
 // Decode (reference model.c:826-850): one query per sequence against its cached
 // positions, read through the page table. Positions are split into 64-position
-// chunks, one block each (flash-decoding); a second kernel merges the chunk
-// partials (max, sum, unnormalised output) in chunk order.
+// chunks, one block each (flash-decoding), and the chunk partials (max, sum,
+// unnormalised output) are merged in chunk order -- by the last block of each
+// (sequence, head) in the fused kernel, or by a second kernel.
 //
 // With statistics enabled (reference model_collect_attn_stats) a second pass
 // recomputes each row's normalised probabilities from the same scores and
 // records the min and max of their double-precision sums.
 #include "common.cuh"
+#include "tc_gemm.h"
 
 #include <cfloat>
 
@@ -36,7 +38,8 @@ __device__ __forceinline__ void stats_update(AttnStats* st, double rowsum) {
 template <bool STATS>
 __global__ void __launch_bounds__(128)
 attn_prefill_kernel(const float* __restrict__ qkv, int T, int H, float scale,
-                    float* __restrict__ out, AttnStats* stats) {
+                    float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo,
+                    AttnStats* stats) {
     extern __shared__ __align__(16) float smem[];
     float* Qs = smem;                  // [BQ][LDS]
     float* Ks = Qs + BQ * LDS;         // [BKEY][LDS]
@@ -182,11 +185,26 @@ attn_prefill_kernel(const float* __restrict__ qkv, int T, int H, float scale,
         const int t = q0 + rows[i];
         if (t < T) {
             const float inv = 1.0f / l_i[i];
-            float* dst = out + ((size_t)seq * T + t) * E + h * D;
-            *reinterpret_cast<float4*>(dst + tx * 4) =
-                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
-            *reinterpret_cast<float4*>(dst + 32 + tx * 4) =
-                make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+            const size_t ob = ((size_t)seq * T + t) * E + h * D;
+            float v[8];
+#pragma unroll
+            for (int d = 0; d < 8; ++d) v[d] = o[i][d] * inv;
+            if (out) {
+                *reinterpret_cast<float4*>(out + ob + tx * 4) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4*>(out + ob + 32 + tx * 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            if (out_hi) {
+                float hv[8], lv[8];
+#pragma unroll
+                for (int d = 0; d < 8; ++d) {
+                    hv[d] = tf32_hi(v[d]);
+                    lv[d] = __fsub_rn(v[d], hv[d]);
+                }
+                *reinterpret_cast<float4*>(out_hi + ob + tx * 4) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4*>(out_hi + ob + 32 + tx * 4) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+                *reinterpret_cast<float4*>(out_lo + ob + tx * 4) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                *reinterpret_cast<float4*>(out_lo + ob + 32 + tx * 4) = make_float4(lv[4], lv[5], lv[6], lv[7]);
+            }
         }
     }
 
@@ -276,6 +294,7 @@ template <bool STATS>
 __global__ void __launch_bounds__(D)
 attn_decode_combine_kernel(const int32_t* __restrict__ lens, int H, int max_splits,
                            const float* __restrict__ part, float* __restrict__ out,
+                           float* __restrict__ out_hi, float* __restrict__ out_lo,
                            const float* __restrict__ e_in, int e_ld, AttnStats* stats) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int ctx = lens[b] + 1;
@@ -289,7 +308,14 @@ attn_decode_combine_kernel(const int32_t* __restrict__ lens, int H, int max_spli
         l = fmaf(pp[s * PART + 1], c, l);
         o = fmaf(pp[s * PART + 2 + d], c, o);
     }
-    out[(size_t)b * H * D + h * D + d] = o / l;
+    const float y = o / l;
+    const size_t oi = (size_t)b * H * D + h * D + d;
+    if (out) out[oi] = y;
+    if (out_hi) {
+        const float hv = tf32_hi(y);
+        out_hi[oi] = hv;
+        out_lo[oi] = __fsub_rn(y, hv);
+    }
     if constexpr (STATS) {
         if (d == 0) {
             const float inv = (float)(1.0 / (double)l);
@@ -305,22 +331,149 @@ attn_decode_combine_kernel(const int32_t* __restrict__ lens, int H, int max_spli
     }
 }
 
+
+// Decode attention, one kernel: each block stages its 64-position chunk of K
+// and V with cp.async (all 16-byte copies in flight at once), computes the
+// chunk's scores, max, exponentials, sum and unnormalised output, and writes
+// them as a partial. The last block of a (sequence, head) to finish -- counted
+// with an atomic -- merges all partials in chunk order (so the result does not
+// depend on which block was last) and resets the counter for the next launch.
+constexpr int KLD = D + 8;  // padded row: conflict-free 16-byte reads
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(128)
+attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int H, PagedKV kv,
+                         int max_splits, float scale, float* __restrict__ part, int* __restrict__ counters,
+                         float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo) {
+    const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int ctx = lens[b] + 1;
+    const int ns = (ctx + CH - 1) / CH;
+    if (s >= ns) return;
+    const int p0 = s * CH, n = min(CH, ctx - p0);
+    const int E = kv.n_embd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ __align__(16) float Ks[CH * KLD];
+    __shared__ __align__(16) float Vs[CH * KLD];
+    __shared__ float s_e[CH];
+    __shared__ float s_red[8][D];
+    __shared__ float s_w[4];
+    __shared__ int s_last;
+
+    // stage K and V: n rows x 16 chunks of 16 bytes each
+    for (int i = tid; i < n * 16; i += 128) {
+        const int r = i >> 4, c = (i & 15) * 4;
+        const size_t row = kv.row(b, p0 + r);
+        cp_async16(&Ks[r * KLD + c], kv.k + row * E + h * D + c);
+        cp_async16(&Vs[r * KLD + c], kv.v + row * E + h * D + c);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // this thread's half of the query: dims 4*(2j + half) .. +3, j = 0..7
+    const int pi = tid >> 1, half = tid & 1;
+    const float* q = qkv + (size_t)b * 3 * E + h * D;
+    float4 qv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qv[j] = *reinterpret_cast<const float4*>(q + 4 * (2 * j + half));
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
+    // scores: two threads per position
+    float a = 0.f;
+    if (pi < n) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 k4 = *reinterpret_cast<const float4*>(&Ks[pi * KLD + 4 * (2 * j + half)]);
+            a = fmaf(qv[j].x, k4.x, a);
+            a = fmaf(qv[j].y, k4.y, a);
+            a = fmaf(qv[j].z, k4.z, a);
+            a = fmaf(qv[j].w, k4.w, a);
+        }
+    }
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    const float sc = pi < n ? a * scale : -INFINITY;
+    // chunk max
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_w[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(s_w[0], s_w[1]), fmaxf(s_w[2], s_w[3]));
+    if (pi < n && half == 0) s_e[pi] = expf(sc - mx);
+    __syncthreads();
+    // chunk sum, in position order (every thread the same value)
+    float l = 0.f;
+    for (int i = 0; i < n; ++i) l += s_e[i];
+    // unnormalised output: 16 threads per position group, 8 groups
+    const int d4 = tid & 15, g = tid >> 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = g; i < n; i += 8) {
+        const float e = s_e[i];
+        const float4 v = *reinterpret_cast<const float4*>(&Vs[i * KLD + 4 * d4]);
+        acc.x = fmaf(e, v.x, acc.x);
+        acc.y = fmaf(e, v.y, acc.y);
+        acc.z = fmaf(e, v.z, acc.z);
+        acc.w = fmaf(e, v.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(&s_red[g][4 * d4]) = acc;
+    __syncthreads();
+    float* pp = part + ((size_t)(b * H + h) * max_splits + s) * PART;
+    if (tid < D) {
+        float o = s_red[0][tid];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) o += s_red[k][tid];
+        pp[2 + tid] = o;
+    }
+    if (tid == 0) { pp[0] = mx; pp[1] = l; }
+
+    // the last block of this (sequence, head) merges the partials
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&counters[b * H + h], 1) == ns - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < D) {
+        const float* base = part + (size_t)(b * H + h) * max_splits * PART;
+        float m = __ldcg(base);
+        for (int k = 1; k < ns; ++k) m = fmaxf(m, __ldcg(base + k * PART));
+        float lt = 0.f, o = 0.f;
+        for (int k = 0; k < ns; ++k) {
+            const float c = expf(__ldcg(base + k * PART) - m);
+            lt = fmaf(__ldcg(base + k * PART + 1), c, lt);
+            o = fmaf(__ldcg(base + k * PART + 2 + tid), c, o);
+        }
+        const float y = o / lt;
+        const size_t oi = (size_t)b * H * D + h * D + tid;
+        if (out) out[oi] = y;
+        if (out_hi) {
+            const float hv = tf32_hi(y);
+            out_hi[oi] = hv;
+            out_lo[oi] = __fsub_rn(y, hv);
+        }
+    }
+    if (tid == 0) counters[b * H + h] = 0;
+}
+
 }  // namespace
 
 int attn_decode_max_splits(int capacity) { return (capacity + CH - 1) / CH; }
 
 cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
-                                AttnStats* stats, cudaStream_t st) {
+                                AttnStats* stats, cudaStream_t st, float* out_hi, float* out_lo) {
     if (T <= 0 || n_seq <= 0) return cudaSuccess;
     const size_t smem = (size_t)(BQ * LDS * 3 + BKEY * (BQ + 4)) * sizeof(float);
     const float scale = (float)(1.0 / sqrt((double)D));
     dim3 grid((T + BQ - 1) / BQ, H, n_seq);
     if (stats) {
         cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_prefill_kernel<true><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, stats);
+        attn_prefill_kernel<true><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, out_hi, out_lo, stats);
     } else {
         cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_prefill_kernel<false><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, nullptr);
+        attn_prefill_kernel<false><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, out_hi, out_lo, nullptr);
     }
     return cudaGetLastError();
 }
@@ -329,7 +482,7 @@ cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float
 // B * H * max_splits * CH floats after the partials for the probabilities.
 cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv,
                                int max_splits, float* part, float* out, AttnStats* stats,
-                               cudaStream_t st) {
+                               cudaStream_t st, float* out_hi, float* out_lo, int* counters) {
     if (B <= 0) return cudaSuccess;
     const float scale = (float)(1.0 / sqrt((double)D));
     dim3 g1(max_splits, H, B), g2(H, B);
@@ -337,10 +490,13 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
         float* e = part + (size_t)B * H * max_splits * PART;
         const int e_ld = max_splits * CH;
         attn_decode_split_kernel<true><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, e, e_ld);
-        attn_decode_combine_kernel<true><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, e, e_ld, stats);
+        attn_decode_combine_kernel<true><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, out_hi, out_lo, e, e_ld, stats);
+    } else if (counters) {
+        attn_decode_fused_kernel<<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, counters, out,
+                                                     out_hi, out_lo);
     } else {
         attn_decode_split_kernel<false><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, nullptr, 0);
-        attn_decode_combine_kernel<false><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, nullptr, 0, nullptr);
+        attn_decode_combine_kernel<false><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, out_hi, out_lo, nullptr, 0, nullptr);
     }
     return cudaGetLastError();
 }

@@ -1,6 +1,7 @@
 // k_misc.cu -- embedding, LayerNorm, KV stores, argmax reductions, greedy-step
 // bookkeeping, the load-time transpose and the naive (reference-order) matmul.
 #include "common.cuh"
+#include "tc_gemm.h"
 
 #include <cfloat>
 #include <climits>
@@ -69,6 +70,7 @@ __global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
 // gain and a float add of the shift, each rounded separately. One warp per row.
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                  const float* __restrict__ bvec, float* __restrict__ y,
+                                 float* __restrict__ y_hi, float* __restrict__ y_lo,
                                  int rows, int E, float eps) {
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -86,10 +88,16 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
     v = warp_sum_d(v);
     v = v / (double)E;
     const float inv = (float)(1.0 / sqrt(__dadd_rn(v, (double)eps)));
-    float* yr = y + (size_t)row * E;
+    const size_t off = (size_t)row * E;
     for (int i = lane; i < E; i += 32) {
         const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
-        yr[i] = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
+        const float v = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
+        if (y) y[off + i] = v;
+        if (y_hi) {
+            const float h = tf32_hi(v);
+            y_hi[off + i] = h;
+            y_lo[off + i] = __fsub_rn(v, h);
+        }
     }
 }
 
@@ -275,10 +283,10 @@ cudaError_t launch_embed_decode(const int32_t* tokens, const int32_t* lens, int 
 }
 
 cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float* y, int rows,
-                             int E, float eps, cudaStream_t st) {
+                             int E, float eps, cudaStream_t st, float* y_hi, float* y_lo) {
     const int warps_per_block = 8;
     const int grid = (rows + warps_per_block - 1) / warps_per_block;
-    layernorm_kernel<<<grid, warps_per_block * 32, 0, st>>>(x, g, b, y, rows, E, eps);
+    layernorm_kernel<<<grid, warps_per_block * 32, 0, st>>>(x, g, b, y, y_hi, y_lo, rows, E, eps);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,403 @@
+// k_tc_gemm.cu -- fp32-accurate matmul on the 5th-generation tensor cores.
+//
+//   C[M,N] (epilogue) = A[M,K] . B[N,K]^T,  A and B K-major fp32
+//
+// Each operand arrives split in two tf32 halves, x = hi + lo with
+// hi = round_to_tf32(x) and lo = x - hi (exact in fp32), and every k-step issues
+// three tcgen05.mma (kind::tf32) into the same fp32 TMEM accumulator:
+// lo(A).hi(B) + hi(A).lo(B) + hi(A).hi(B). The dropped lo.lo term and the tf32
+// rounding of the lo halves leave a relative error near 2^-21 per product --
+// fp32-level, where a plain tf32 product would be near 2^-11. (The split is the
+// published "3xTF32" scheme.)
+//
+// Structure (one 128 x BN output tile per CTA, 192 threads):
+//   warp 0      TMA producer: 4 tiles per 32-wide k-block (A hi/lo, B hi/lo),
+//               128-byte swizzled, into a STAGES-deep shared-memory ring
+//   warp 1      allocates the TMEM accumulator and issues the MMAs (one thread),
+//               committing each stage back to the producer
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32 TMEM
+//               lanes), apply bias / GELU / residual, store fp32 and/or the
+//               hi/lo split the next matmul consumes
+// A grid z-dimension splits K: each split writes raw partial sums that
+// tc_splitk_reduce adds in split order (deterministic) and finishes with the
+// epilogue. The split count depends only on N and K, never on M, so a row's
+// result does not depend on how many rows are in the batch.
+//
+// Every wait on an mbarrier is bounded; on expiry the kernel records an error
+// flag, still drains its own TMA copies and MMAs, frees its TMEM and returns.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "tc_gemm.h"
+
+namespace tie {
+namespace {
+
+constexpr int BM = 128, BK = 32;
+constexpr int THREADS = 192;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: false (and the error flag set) if the phase has not completed
+// within kWaitLimitNs of wall time.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    atomicExch(err, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
+                                            int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 bytes
+// in 8-row (1024-byte) groups. Start address and strides in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    const uint64_t start = (addr >> 4) & 0x3FFFu;
+    const uint64_t lbo = 1;          // unused for swizzled K-major
+    const uint64_t sbo = 1024 >> 4;  // between 8-row groups
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (2ull << 61) /* SW128 */;
+}
+
+// kind::tf32 instruction descriptor: fp32 accumulate, tf32 A and B, both
+// K-major, M = 128, N = BN.
+template <int BN>
+__device__ __forceinline__ uint32_t idesc_tf32() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+          "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+          "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN>
+constexpr size_t stage_bytes() { return 2 * (size_t)BM * 128 + 2 * (size_t)BN * 128; }
+
+template <int BN>
+constexpr int stages() { return BN >= 256 ? 2 : 3; }
+
+template <int BN>
+constexpr size_t smem_bytes() {
+    return 1024 /* alignment slack */ + stages<BN>() * stage_bytes<BN>() + 256 /* barriers */;
+}
+
+template <int BN, int EPI, int OUT>
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+               const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+               TcArgs p) {
+    constexpr int S = stages<BN>();
+    constexpr uint32_t kStageBytes = (uint32_t)stage_bytes<BN>();
+    constexpr uint32_t kTileA = BM * 128, kTileB = BN * 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+    uint64_t* full = bars;            // [S]
+    uint64_t* empty = bars + S;       // [S]
+    uint64_t* accum = bars + 2 * S;   // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int kb0 = blockIdx.z * p.kb_per_split;
+    const int nkb = min(p.kb_per_split, p.K / BK - kb0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        mbar_init(smem_u32(accum), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (uint32_t)((kb / S) & 1);
+                if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) break;
+                const uint32_t base = smem_u32(smem + s * kStageBytes);
+                const uint32_t fb = smem_u32(&full[s]);
+                mbar_expect_tx(fb, kStageBytes);
+                const int kx = (kb0 + kb) * BK;
+                tma_load_2d(base, &ta_hi, fb, kx, m0);
+                tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
+                tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
+                tma_load_2d(base + 2 * kTileA + kTileB, &tb_lo, fb, kx, n0);
+                ++issued;
+            }
+            // drain: every copy this thread started has landed before exit
+            for (int kb = max(0, issued - S); kb < issued; ++kb)
+                mbar_wait(smem_u32(&full[kb % S]), (uint32_t)((kb / S) & 1), p.err);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32<BN>();
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((kb / S) & 1), p.err)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t base = smem_u32(smem + s * kStageBytes);
+#pragma unroll
+                for (int j = 0; j < BK / 8; ++j) {  // 4 k-steps of 8 tf32 (32 bytes) each
+                    const uint64_t a_hi = sw128_desc(base + j * 32);
+                    const uint64_t a_lo = sw128_desc(base + kTileA + j * 32);
+                    const uint64_t b_hi = sw128_desc(base + 2 * kTileA + j * 32);
+                    const uint64_t b_lo = sw128_desc(base + 2 * kTileA + kTileB + j * 32);
+                    mma_tf32(tmem, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    mma_tf32(tmem, a_hi, b_lo, idesc, 1u);
+                    mma_tf32(tmem, a_hi, b_hi, idesc, 1u);
+                }
+                mma_commit(smem_u32(&empty[s]));
+            }
+            // arrives once every MMA issued above has completed (also on the error path)
+            mma_commit(smem_u32(accum));
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int q = warp & 3;  // this warp's TMEM lane quarter
+        const bool ok = mbar_wait(smem_u32(accum), 0u, p.err) && nkb > 0;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const int row = m0 + q * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+            if (!ok || row >= p.M) continue;
+            const int col0 = n0 + c * 32;
+            if constexpr (OUT == TC_OUT_PARTIAL) {
+                float* dst = p.partial + ((size_t)blockIdx.z * p.M + row) * p.N + col0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (col0 + i < p.N) dst[i] = __uint_as_float(r[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = col0 + i;
+                    if (col >= p.N) continue;
+                    const size_t o = (size_t)row * p.ldc + col;
+                    const float y = apply_epi<EPI>(__uint_as_float(r[i]), p.bias, col, p.C + o);
+                    if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o] = y;
+                    if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
+                        const float hi = tf32_hi(y);
+                        p.C_hi[o] = hi;
+                        p.C_lo[o] = __fsub_rn(y, hi);
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+    }
+}
+
+// Sum of the split partials in split order, then the epilogue.
+template <int EPI, int OUT>
+__global__ void tc_splitk_reduce(TcArgs p, int splits) {
+    const long long n = (long long)p.M * p.N;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / p.N), col = (int)(i % p.N);
+        float acc = p.partial[i];
+        for (int z = 1; z < splits; ++z) acc = __fadd_rn(acc, p.partial[(size_t)z * n + i]);
+        const size_t o = (size_t)row * p.ldc + col;
+        const float y = apply_epi<EPI>(acc, p.bias, col, p.C + o);
+        if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o] = y;
+        if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
+            const float hi = tf32_hi(y);
+            p.C_hi[o] = hi;
+            p.C_lo[o] = __fsub_rn(y, hi);
+        }
+    }
+}
+
+__global__ void split_hilo_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const float h = tf32_hi(v);
+        hi[i] = h;
+        lo[i] = __fsub_rn(v, h);
+    }
+}
+
+using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point.
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 2-D map over a rows x cols fp32 matrix (row stride ld floats), box 32 x box_rows.
+bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI, int OUT>
+cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStream_t st) {
+    CUtensorMap m[4];
+    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, BM) || !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, BM) ||
+        !make_map(&m[2], op.b_hi, a.N, a.K, op.ldb, BN) || !make_map(&m[3], op.b_lo, a.N, a.K, op.ldb, BN))
+        return cudaErrorInvalidValue;
+    constexpr size_t smem = smem_bytes<BN>();
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, OUT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM, splits);
+    tc_gemm_kernel<BN, EPI, OUT><<<grid, THREADS, smem, st>>>(m[0], m[1], m[2], m[3], a);
+    return cudaGetLastError();
+}
+
+template <int EPI, int OUT>
+cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
+    if (splits <= 1) {
+        a.kb_per_split = a.K / BK;
+        return launch_bn<128, EPI, OUT>(op, a, 1, st);
+    }
+    a.kb_per_split = (a.K / BK + splits - 1) / splits;
+    const int used = (a.K / BK + a.kb_per_split - 1) / a.kb_per_split;
+    cudaError_t e = launch_bn<128, EPI_STORE, TC_OUT_PARTIAL>(op, a, used, st);
+    if (e != cudaSuccess) return e;
+    const long long n = (long long)a.M * a.N;
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 16);
+    tc_splitk_reduce<EPI, OUT><<<grid, 256, 0, st>>>(a, used);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
+    return M > 0 && N > 0 && K > 0 && K % BK == 0 && lda % 4 == 0 && ldb % 4 == 0 && encode_fn() != nullptr;
+}
+
+// Split count for a decode-sized matmul: enough blocks to cover the SMs,
+// chosen from N and K only.
+int tc_splits_for(int N, int K) {
+    const int n_tiles = (N + 127) / 128;
+    const int kb = K / BK;
+    int s = 1;
+    while (n_tiles * s * 2 <= 148 && s * 2 <= kb / 4) s *= 2;
+    return s;
+}
+
+cudaError_t launch_tc_gemm(const TcOperands& op, const TcArgs& a, int epi, int out, int splits,
+                           cudaStream_t st) {
+    if (!tc_gemm_supported(a.M, a.N, a.K, op.lda, op.ldb)) return cudaErrorInvalidValue;
+    if (splits > 1 && !a.partial) return cudaErrorInvalidValue;
+#define TC_CASE(E, O) \
+    if (epi == E && out == O) return launch_epi<E, O>(op, a, splits, st);
+    TC_CASE(EPI_STORE, TC_OUT_F32)
+    TC_CASE(EPI_BIAS, TC_OUT_F32)
+    TC_CASE(EPI_BIAS_RESID, TC_OUT_F32)
+    TC_CASE(EPI_BIAS_GELU, TC_OUT_HILO)
+    TC_CASE(EPI_BIAS_GELU, TC_OUT_F32_HILO)
+    TC_CASE(EPI_BIAS_GELU, TC_OUT_F32)
+#undef TC_CASE
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_split_hilo(const float* x, float* hi, float* lo, long long n, cudaStream_t st) {
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 32);
+    split_hilo_kernel<<<grid > 0 ? grid : 1, 256, 0, st>>>(x, hi, lo, n);
+    return cudaGetLastError();
+}
+
+}  // namespace tie

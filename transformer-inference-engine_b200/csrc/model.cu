@@ -16,6 +16,7 @@
 #include "../../include/safetensors.h"
 #include "../../include/tie_b200.h"
 #include "internal.h"
+#include "tc_gemm.h"
 
 #include <cmath>
 #include <cstdio>
@@ -132,7 +133,20 @@ bool inventory_find(const std::string& inv, const char* name, InvEntry* e) {
 struct Layer {
     float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
     float *ln2_w, *ln2_b, *fc_w, *fc_b, *mlp_w, *mlp_b;
+    // tf32 splits (hi + lo == the fp32 weight) of the four matrices, for the
+    // tensor-core matmul
+    float *qkv_hi, *qkv_lo, *proj_hi, *proj_lo, *fc_hi, *fc_lo, *mlp_hi, *mlp_lo;
 };
+
+// A matmul operand: its fp32 values and/or its tf32 split.
+struct Mat {
+    const float* f;
+    const float* hi;
+    const float* lo;
+};
+
+// Decode batches of at most this many rows take the streaming GEMV.
+constexpr int kGemvRows = 16;
 
 // One instantiated decode graph per (batch size, cache, advance, output) key,
 // with the number of kernels one replay runs.
@@ -168,13 +182,21 @@ struct model {
 
     float* d_weights = nullptr;
     size_t weight_bytes = 0;
+    float* d_split = nullptr;  // tf32 splits of every matrix
+    size_t split_bytes = 0;
     float *wte = nullptr, *wpe = nullptr, *lnf_w = nullptr, *lnf_b = nullptr;
+    float *wte_hi = nullptr, *wte_lo = nullptr;
     std::vector<Layer> layers;
     std::vector<model_tensor_record> records;
 
     // activation scratch: `rows` rows
     size_t rows = 0;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr;
+    float *xb_hi = nullptr, *xb_lo = nullptr, *attn_hi = nullptr, *attn_lo = nullptr;
+    float *ff_hi = nullptr, *ff_lo = nullptr;
+    size_t partial_floats = 0;
+    float* d_partial = nullptr;  // split-K workspace of the decode matmuls
+    int* d_err = nullptr;        // set by a kernel whose bounded wait expired
     size_t logit_rows = 0;
     float* logits = nullptr;
     size_t ids_cap = 0;
@@ -187,6 +209,8 @@ struct model {
     int32_t* d_out = nullptr;
     size_t part_floats = 0;
     float* d_part = nullptr;
+    size_t cnt_cap = 0;
+    int* d_attn_cnt = nullptr;  // per (sequence, head) arrival counters of the decode attention
     size_t am_parts = 0;
     float* d_am_val = nullptr;
     int* d_am_idx = nullptr;
@@ -237,20 +261,26 @@ model_status grow(T** p, size_t* cap, size_t need) {
 }
 
 model_status ensure_rows(model* m, size_t rows) {
+    if (!m->d_err) {
+        CU(cudaMalloc(&m->d_err, sizeof(int)));
+        CU(cudaMemset(m->d_err, 0, sizeof(int)));
+    }
     if (rows <= m->rows) return MODEL_OK;
     drop_graphs(m);
     const size_t E = (size_t)m->cfg.n_embd;
-    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr;
-    if (cudaMalloc(&x, rows * E * 4) != cudaSuccess || cudaMalloc(&xb, rows * E * 4) != cudaSuccess ||
-        cudaMalloc(&qkv, rows * 3 * E * 4) != cudaSuccess ||
-        cudaMalloc(&attn, rows * E * 4) != cudaSuccess ||
-        cudaMalloc(&ff, rows * 4 * E * 4) != cudaSuccess) {
+    // per row: x, xb, qkv (3E), attn, ff (4E), xb hi/lo, attn hi/lo, ff hi/lo (8E)
+    const size_t per_row = E * (1 + 1 + 3 + 1 + 4 + 2 + 2 + 8);
+    float* block = nullptr;
+    if (cudaMalloc(&block, rows * per_row * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
-        cudaFree(x); cudaFree(xb); cudaFree(qkv); cudaFree(attn); cudaFree(ff);
         return MODEL_ERR_NOMEM;
     }
-    cudaFree(m->x); cudaFree(m->xb); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->ff);
-    m->x = x; m->xb = xb; m->qkv = qkv; m->attn = attn; m->ff = ff;
+    cudaFree(m->x);
+    float* c = block;
+    auto take = [&](size_t w) { float* p = c; c += rows * w; return p; };
+    m->x = take(E); m->xb = take(E); m->qkv = take(3 * E); m->attn = take(E); m->ff = take(4 * E);
+    m->xb_hi = take(E); m->xb_lo = take(E); m->attn_hi = take(E); m->attn_lo = take(E);
+    m->ff_hi = take(4 * E); m->ff_lo = take(4 * E);
     m->rows = rows;
     return grow(&m->d_ids, &m->ids_cap, rows);
 }
@@ -294,6 +324,12 @@ model_status ensure_slots(model* m, size_t B, int capacity) {
         drop_graphs(m);
         if ((rc = grow(&m->d_part, &m->part_floats, need)) != MODEL_OK) return rc;
     }
+    const size_t cnt = B * (size_t)m->cfg.n_head;
+    if (cnt > m->cnt_cap) {
+        drop_graphs(m);
+        if ((rc = grow(&m->d_attn_cnt, &m->cnt_cap, cnt)) != MODEL_OK) return rc;
+        CU(cudaMemset(m->d_attn_cnt, 0, cnt * sizeof(int)));
+    }
     const size_t parts = (size_t)gemv_argmax_blocks(m->cfg.vocab_size) * B;
     if (parts > m->am_parts) {
         drop_graphs(m);
@@ -303,7 +339,43 @@ model_status ensure_slots(model* m, size_t B, int capacity) {
         m->am_parts = parts;
     }
     if ((rc = ensure_logits(m, B)) != MODEL_OK) return rc;
+    if (B > (size_t)kGemvRows) {
+        const int E = m->cfg.n_embd;
+        const int shapes[5][2] = {{3 * E, E}, {E, E}, {4 * E, E}, {E, 4 * E}, {m->cfg.vocab_size, E}};
+        size_t need_p = 0;
+        for (auto& sh : shapes) {
+            const int sp = tc_splits_for(sh[0], sh[1]);
+            if (sp > 1) need_p = std::max(need_p, (size_t)sp * B * (size_t)sh[0]);
+        }
+        if (need_p > m->partial_floats) {
+            drop_graphs(m);
+            if ((rc = grow(&m->d_partial, &m->partial_floats, need_p)) != MODEL_OK) return rc;
+        }
+    }
     return ensure_pinned(m, 2 * B + 16);
+}
+
+// Y (epilogue) = X . W^T over `rows` rows. Decode batches of at most kGemvRows
+// rows take the streaming GEMV on fp32 operands; everything else takes the
+// tensor-core matmul on tf32 splits (split over K, by N and K only, for
+// decode-sized calls). Outputs: y (fp32) and/or y_hi/y_lo (its split).
+model_status matmul(model* m, bool decode, int rows, Mat x, int ldx, Mat w, int N, int K,
+                    const float* bias, int epi, float* y, float* y_hi, float* y_lo, int ldy) {
+    cudaStream_t st = m->st;
+    if (decode && rows <= kGemvRows) {
+        LAUNCH(launch_gemv(x.f, ldx, w.f, K, bias, y, ldy, rows, N, K, epi, st));
+        return MODEL_OK;
+    }
+    TcOperands op{x.hi, x.lo, ldx, w.hi, w.lo, K};
+    TcArgs a{};
+    a.M = rows; a.N = N; a.K = K; a.bias = bias;
+    a.C = y; a.C_hi = y_hi; a.C_lo = y_lo; a.ldc = ldy;
+    a.partial = m->d_partial; a.err = m->d_err;
+    const int out = y_hi ? (y ? TC_OUT_F32_HILO : TC_OUT_HILO) : TC_OUT_F32;
+    const int splits = decode ? tc_splits_for(N, K) : 1;
+    LAUNCH(launch_tc_gemm(op, a, epi, out, splits, st));
+    if (splits > 1) ++m->launches;  // the split reduction
+    return MODEL_OK;
 }
 
 // ------------------------------------------------------------- stats --
@@ -343,20 +415,40 @@ model_status run_prefill(model* m, int n_seq, int T, kv_cache* cache, int first_
     const float eps = m->cfg.layer_norm_epsilon;
     cudaStream_t st = m->st;
     AttnStats* stats = m->stats_on ? m->d_stats : nullptr;
+    const Mat xb{nullptr, m->xb_hi, m->xb_lo}, attn{nullptr, m->attn_hi, m->attn_lo};
+    const Mat ff{nullptr, m->ff_hi, m->ff_lo};
+    model_status rc;
     LAUNCH(launch_embed_prefill(m->d_ids, R, T, m->wte, m->wpe, m->x, E, m->cfg.vocab_size, st));
     for (int l = 0; l < m->cfg.n_layer; ++l) {
         const Layer& w = m->layers[l];
-        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, m->xb, R, E, eps, st));
-        LAUNCH(launch_gemm_tn(m->xb, E, w.qkv_w, E, w.qkv_b, m->qkv, 3 * E, R, 3 * E, E, EPI_BIAS, st));
+        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, nullptr, R, E, eps, st, m->xb_hi, m->xb_lo));
+        if ((rc = matmul(m, false, R, xb, E, Mat{w.qkv_w, w.qkv_hi, w.qkv_lo}, 3 * E, E, w.qkv_b, EPI_BIAS,
+                         m->qkv, nullptr, nullptr, 3 * E)) != MODEL_OK)
+            return rc;
         if (cache) LAUNCH(launch_kv_store_prefill(m->qkv, n_seq, T, layer_view(cache, l), first_seq, st));
-        LAUNCH(launch_attn_prefill(m->qkv, n_seq, T, H, m->attn, stats, st));
-        LAUNCH(launch_gemm_tn(m->attn, E, w.proj_w, E, w.proj_b, m->x, E, R, E, E, EPI_BIAS_RESID, st));
-        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, R, E, eps, st));
-        LAUNCH(launch_gemm_tn(m->xb, E, w.fc_w, E, w.fc_b, m->ff, 4 * E, R, 4 * E, E, EPI_BIAS_GELU, st));
-        LAUNCH(launch_gemm_tn(m->ff, 4 * E, w.mlp_w, 4 * E, w.mlp_b, m->x, E, R, E, 4 * E, EPI_BIAS_RESID, st));
+        LAUNCH(launch_attn_prefill(m->qkv, n_seq, T, H, nullptr, stats, st, m->attn_hi, m->attn_lo));
+        if ((rc = matmul(m, false, R, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
+                         EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
+            return rc;
+        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, nullptr, R, E, eps, st, m->xb_hi, m->xb_lo));
+        if ((rc = matmul(m, false, R, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
+                         nullptr, m->ff_hi, m->ff_lo, 4 * E)) != MODEL_OK)
+            return rc;
+        if ((rc = matmul(m, false, R, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
+                         EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
+            return rc;
     }
-    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, R, E, eps, st));
+    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, nullptr, R, E, eps, st, m->xb_hi, m->xb_lo));
     return MODEL_OK;
+}
+
+// The tied head over `rows` rows of LN_f(x) starting at row `first` with row
+// stride `stride` rows: logits [rows, V] into m->logits.
+model_status prefill_head(model* m, int rows, size_t first, int stride) {
+    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    const size_t off = first * (size_t)E;
+    return matmul(m, false, rows, Mat{nullptr, m->xb_hi + off, m->xb_lo + off}, stride * E,
+                  Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr, EPI_STORE, m->logits, nullptr, nullptr, V);
 }
 
 // One decode step for B sequences: token d_tokens[b] at position d_lens[b],
@@ -370,32 +462,47 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
     cudaStream_t st = m->st;
     AttnStats* stats = m->stats_on ? m->d_stats : nullptr;
     const int max_splits = attn_decode_max_splits(cache->capacity);
-    const bool small = B <= 16;
-    auto mm = [&](const float* X, int ldx, const float* Wt, const float* bias, float* Y, int ldy,
-                  int N, int K, int epi) -> cudaError_t {
-        return small ? launch_gemv(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st)
-                     : launch_gemm_tn(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st);
-    };
+    const bool small = B <= kGemvRows;
+    // GEMV batches carry fp32 activations, tensor-core batches their tf32 splits
+    float* xb_f = small ? m->xb : nullptr;
+    float* xb_h = small ? nullptr : m->xb_hi;
+    float* xb_l = small ? nullptr : m->xb_lo;
+    const Mat xb{m->xb, m->xb_hi, m->xb_lo}, attn{m->attn, m->attn_hi, m->attn_lo};
+    const Mat ff{m->ff, m->ff_hi, m->ff_lo};
+    model_status rc;
     LAUNCH(launch_embed_decode(m->d_tokens, m->d_lens, B, m->wte, m->wpe, m->x, E, V, st));
     for (int l = 0; l < m->cfg.n_layer; ++l) {
         const Layer& w = m->layers[l];
         const PagedKV view = layer_view(cache, l);
-        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, m->xb, B, E, eps, st));
-        LAUNCH(mm(m->xb, E, w.qkv_w, w.qkv_b, m->qkv, 3 * E, 3 * E, E, EPI_BIAS));
+        LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, xb_f, B, E, eps, st, xb_h, xb_l));
+        if ((rc = matmul(m, true, B, xb, E, Mat{w.qkv_w, w.qkv_hi, w.qkv_lo}, 3 * E, E, w.qkv_b, EPI_BIAS,
+                         m->qkv, nullptr, nullptr, 3 * E)) != MODEL_OK)
+            return rc;
         LAUNCH(launch_kv_store_decode(m->qkv, m->d_lens, B, view, st));
-        LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st));
-        ++m->launches;  // the combine kernel
-        LAUNCH(mm(m->attn, E, w.proj_w, w.proj_b, m->x, E, E, E, EPI_BIAS_RESID));
-        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, B, E, eps, st));
-        LAUNCH(mm(m->xb, E, w.fc_w, w.fc_b, m->ff, 4 * E, 4 * E, E, EPI_BIAS_GELU));
-        LAUNCH(mm(m->ff, 4 * E, w.mlp_w, w.mlp_b, m->x, E, E, 4 * E, EPI_BIAS_RESID));
+        LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part,
+                                  small ? m->attn : nullptr, stats, st, small ? nullptr : m->attn_hi,
+                                  small ? nullptr : m->attn_lo, m->d_attn_cnt));
+        if (stats) ++m->launches;  // the separate merge kernel
+        if ((rc = matmul(m, true, B, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
+                         EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
+            return rc;
+        LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, xb_f, B, E, eps, st, xb_h, xb_l));
+        if ((rc = matmul(m, true, B, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
+                         small ? m->ff : nullptr, small ? nullptr : m->ff_hi, small ? nullptr : m->ff_lo,
+                         4 * E)) != MODEL_OK)
+            return rc;
+        if ((rc = matmul(m, true, B, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
+                         EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
+            return rc;
     }
-    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, B, E, eps, st));
+    LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, xb_f, B, E, eps, st, xb_h, xb_l));
     if (small) {
         LAUNCH(launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val, m->d_am_idx, st));
         LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, gemv_argmax_blocks(V), B, m->d_next, st));
     } else {
-        LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, B, V, E, EPI_STORE, st));
+        if ((rc = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr, EPI_STORE,
+                         m->logits, nullptr, nullptr, V)) != MODEL_OK)
+            return rc;
         LAUNCH(launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st));
     }
     if (advance) LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
@@ -448,6 +555,14 @@ model_status set_slot_state(model* m, size_t B, const int32_t* tokens, const int
 
 model_status finish(model* m) {
     CU(cudaStreamSynchronize(m->st));
+    if (m->d_err) {
+        int err = 0;
+        CU(cudaMemcpy(&err, m->d_err, sizeof err, cudaMemcpyDeviceToHost));
+        if (err) {
+            cudaMemset(m->d_err, 0, sizeof(int));
+            return MODEL_ERR_DEVICE;
+        }
+    }
     return stats_end(m);
 }
 
@@ -673,6 +788,36 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
                                "[input, output] as stored; held [output, input] on the device");
             TRY(vec("h.%d.mlp.c_proj.bias", E, &y.mlp_b));
         }
+        // tf32 splits of every matrix, for the tensor-core matmul
+        {
+            const size_t mats = V * E + L * (3 * E * E + E * E + 4 * E * E + 4 * E * E);
+            m->split_bytes = 2 * mats * sizeof(float);
+            if (cudaMalloc(&m->d_split, m->split_bytes) != cudaSuccess) {
+                cudaGetLastError();
+                rc = MODEL_ERR_NOMEM;
+                goto fail;
+            }
+            float* sc = m->d_split;
+            auto split = [&](const float* src, size_t n, float** hi, float** lo) -> model_status {
+                *hi = sc;
+                *lo = sc + n;
+                sc += 2 * n;
+                CU(launch_split_hilo(src, *hi, *lo, (long long)n, nullptr));
+                return MODEL_OK;
+            };
+            TRY(split(m->wte, V * E, &m->wte_hi, &m->wte_lo));
+            for (auto& y : m->layers) {
+                TRY(split(y.qkv_w, 3 * E * E, &y.qkv_hi, &y.qkv_lo));
+                TRY(split(y.proj_w, E * E, &y.proj_hi, &y.proj_lo));
+                TRY(split(y.fc_w, 4 * E * E, &y.fc_hi, &y.fc_lo));
+                TRY(split(y.mlp_w, 4 * E * E, &y.mlp_hi, &y.mlp_lo));
+            }
+            if (cudaDeviceSynchronize() != cudaSuccess) {
+                cudaGetLastError();
+                rc = MODEL_ERR_DEVICE;
+                goto fail;
+            }
+        }
 #undef TRY
     }
     cudaFree(staging);
@@ -727,10 +872,13 @@ void model_free(model* m) {
     if (m->st) cudaStreamSynchronize(m->st);
     drop_graphs(m);
     cudaFree(m->d_weights);
-    cudaFree(m->x); cudaFree(m->xb); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->ff);
+    cudaFree(m->d_split);
+    cudaFree(m->x);  // the activation block (x, xb, qkv, attn, ff and their splits)
+    cudaFree(m->d_partial);
+    cudaFree(m->d_err);
     cudaFree(m->logits); cudaFree(m->d_ids);
     cudaFree(m->d_tokens); cudaFree(m->d_lens); cudaFree(m->d_next); cudaFree(m->d_step);
-    cudaFree(m->d_out); cudaFree(m->d_part); cudaFree(m->d_am_val); cudaFree(m->d_am_idx);
+    cudaFree(m->d_out); cudaFree(m->d_part); cudaFree(m->d_attn_cnt); cudaFree(m->d_am_val); cudaFree(m->d_am_idx);
     cudaFree(m->d_stats);
     if (m->h_small) cudaFreeHost(m->h_small);
     kv_cache_destroy(m->kv);
@@ -861,7 +1009,7 @@ model_status model_prefill(model* m, const int32_t* ids, size_t T, float* logits
     if ((rc = run_prefill(m, 1, (int)T, use_cache ? m->kv : nullptr, 0)) != MODEL_OK) return rc;
     const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
     // the tied head at every position (model.c:778-780)
-    LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, (int)T, V, E, EPI_STORE, m->st));
+    if ((rc = prefill_head(m, (int)T, 0, 1)) != MODEL_OK) return rc;
     CU(cudaMemcpyAsync(logits, m->logits, T * (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
     if ((rc = finish(m)) != MODEL_OK) return rc;
     if (use_cache) kv_cache_set_length(m->kv, (int)T);
@@ -925,8 +1073,7 @@ model_status model_decode_step(model* m, const int32_t* ids, size_t T, float* lo
     if ((rc = run_prefill(m, 1, (int)T, nullptr, 0)) != MODEL_OK) return rc;
     const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
     // the head at the last position only, with prefill's kernel (model.c:913-916)
-    LAUNCH(launch_gemm_tn(m->xb + (T - 1) * (size_t)E, E, m->wte, E, nullptr, m->logits, V, 1, V, E,
-                          EPI_STORE, m->st));
+    if ((rc = prefill_head(m, 1, T - 1, 1)) != MODEL_OK) return rc;
     CU(cudaMemcpyAsync(logits, m->logits, (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
     return finish(m);
 }
@@ -934,7 +1081,7 @@ model_status model_decode_step(model* m, const int32_t* ids, size_t T, float* lo
 // ----------------------------------------------------------------- batches --
 int model_device(const model* m) { return m ? m->device : -1; }
 void* model_stream(const model* m) { return m ? (void*)m->st : nullptr; }
-size_t model_weight_device_bytes(const model* m) { return m ? m->weight_bytes : 0; }
+size_t model_weight_device_bytes(const model* m) { return m ? m->weight_bytes + m->split_bytes : 0; }
 uint64_t model_kernel_launches(const model* m) { return m ? m->launches : 0; }
 
 model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
@@ -968,14 +1115,13 @@ static model_status batch_prefill_impl(model* m, size_t n_seq, size_t T, float* 
     if ((rc = run_prefill(m, (int)n_seq, (int)T, m->pool, 0)) != MODEL_OK) return rc;
     if (logits_host) {
         if ((rc = ensure_logits(m, n_seq * T)) != MODEL_OK) return rc;
-        LAUNCH(launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, (int)(n_seq * T), V, E, EPI_STORE, m->st));
+        if ((rc = prefill_head(m, (int)(n_seq * T), 0, 1)) != MODEL_OK) return rc;
         CU(cudaMemcpyAsync(logits_host, m->logits, n_seq * T * (size_t)V * sizeof(float),
                            cudaMemcpyDeviceToHost, m->st));
         LAUNCH(launch_argmax_rows(m->logits, V, (int)n_seq, V, (int)T, (int)T - 1, m->d_next, m->st));
     } else {
         // head only at each sequence's last position: rows (T-1) + s*T of xb
-        LAUNCH(launch_gemm_tn(m->xb + (T - 1) * (size_t)E, (int)(T * E), m->wte, E, nullptr, m->logits, V,
-                              (int)n_seq, V, E, EPI_STORE, m->st));
+        if ((rc = prefill_head(m, (int)n_seq, T - 1, (int)T)) != MODEL_OK) return rc;
         LAUNCH(launch_argmax_rows(m->logits, V, (int)n_seq, V, 1, 0, m->d_next, m->st));
     }
     (void)next_host;
@@ -1078,7 +1224,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
     if (!m || !avg_ms || rows == 0 || context == 0 || iters <= 0) return MODEL_ERR_ARG;
     if (!m->pool || (int)rows > m->pool->n_seq || (int)context > m->pool->capacity) return MODEL_ERR_CAPACITY;
     const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size, B = (int)rows;
-    const bool small = B <= 16;
+    const bool small = B <= kGemvRows;
     cudaStream_t st = m->st;
     model_status rc = ensure_slots(m, rows, m->pool->capacity);
     if (rc != MODEL_OK) return rc;
@@ -1094,43 +1240,56 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
     const Layer& w = m->layers[0];
     const PagedKV view = layer_view(m->pool, 0);
     const int splits = attn_decode_max_splits(m->pool->capacity);
-    auto once = [&]() -> cudaError_t {
-        auto mm = [&](const float* X, int ldx, const float* Wt, const float* bias, float* Y, int ldy, int N,
-                      int K, int epi) {
-            return small ? launch_gemv(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st)
-                         : launch_gemm_tn(X, ldx, Wt, K, bias, Y, ldy, B, N, K, epi, st);
-        };
+    const Mat xb{m->xb, m->xb_hi, m->xb_lo}, ff{m->ff, m->ff_hi, m->ff_lo};
+    CU(cudaMemsetAsync(m->xb_hi, 0, R * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->xb_lo, 0, R * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->ff_hi, 0, R * 4 * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->ff_lo, 0, R * 4 * E * sizeof(float), st));
+    auto once = [&]() -> model_status {
         switch (kernel) {
             case TIE_KERNEL_DECODE_ATTENTION:
-                return launch_attn_decode(m->qkv, m->d_lens, B, H, view, splits, m->d_part, m->attn, nullptr, st);
-            case TIE_KERNEL_DECODE_QKV: return mm(m->xb, E, w.qkv_w, w.qkv_b, m->qkv, 3 * E, 3 * E, E, EPI_BIAS);
-            case TIE_KERNEL_DECODE_FC: return mm(m->xb, E, w.fc_w, w.fc_b, m->ff, 4 * E, 4 * E, E, EPI_BIAS_GELU);
+                CU(launch_attn_decode(m->qkv, m->d_lens, B, H, view, splits, m->d_part, small ? m->attn : nullptr,
+                                      nullptr, st, small ? nullptr : m->attn_hi, small ? nullptr : m->attn_lo,
+                                      m->d_attn_cnt));
+                return MODEL_OK;
+            case TIE_KERNEL_DECODE_QKV:
+                return matmul(m, true, B, xb, E, Mat{w.qkv_w, w.qkv_hi, w.qkv_lo}, 3 * E, E, w.qkv_b, EPI_BIAS,
+                              m->qkv, nullptr, nullptr, 3 * E);
+            case TIE_KERNEL_DECODE_FC:
+                return matmul(m, true, B, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
+                              small ? m->ff : nullptr, small ? nullptr : m->ff_hi, small ? nullptr : m->ff_lo,
+                              4 * E);
             case TIE_KERNEL_DECODE_MLP_PROJ:
-                return mm(m->ff, 4 * E, w.mlp_w, w.mlp_b, m->x, E, E, 4 * E, EPI_BIAS_RESID);
+                return matmul(m, true, B, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
+                              EPI_BIAS_RESID, m->x, nullptr, nullptr, E);
             case TIE_KERNEL_DECODE_HEAD:
                 if (small) {
-                    cudaError_t e = launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val,
-                                                       m->d_am_idx, st);
-                    return e != cudaSuccess ? e
-                                            : launch_argmax_finalize(m->d_am_val, m->d_am_idx,
-                                                                     gemv_argmax_blocks(V), B, m->d_next, st);
+                    CU(launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val, m->d_am_idx, st));
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, gemv_argmax_blocks(V), B, m->d_next, st));
+                    return MODEL_OK;
                 } else {
-                    cudaError_t e = launch_gemm_tn(m->xb, E, m->wte, E, nullptr, m->logits, V, B, V, E, EPI_STORE, st);
-                    return e != cudaSuccess ? e : launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st);
+                    model_status r = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr,
+                                            EPI_STORE, m->logits, nullptr, nullptr, V);
+                    if (r != MODEL_OK) return r;
+                    CU(launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st));
+                    return MODEL_OK;
                 }
             case TIE_KERNEL_PREFILL_ATTENTION:
-                return launch_attn_prefill(m->qkv, B, (int)context, H, m->attn, nullptr, st);
+                CU(launch_attn_prefill(m->qkv, B, (int)context, H, nullptr, nullptr, st, m->attn_hi, m->attn_lo));
+                return MODEL_OK;
             case TIE_KERNEL_PREFILL_FC:
-                return launch_gemm_tn(m->xb, E, w.fc_w, E, w.fc_b, m->ff, 4 * E, (int)R, 4 * E, E, EPI_BIAS_GELU, st);
+                return matmul(m, false, (int)R, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b,
+                              EPI_BIAS_GELU, nullptr, m->ff_hi, m->ff_lo, 4 * E);
         }
-        return cudaErrorInvalidValue;
+        return MODEL_ERR_ARG;
     };
-    CU(once());  // warm
+    if ((rc = once()) != MODEL_OK) return rc;  // warm
     cudaEvent_t a, b;
     CU(cudaEventCreate(&a));
     CU(cudaEventCreate(&b));
     CU(cudaEventRecord(a, st));
-    for (int i = 0; i < iters; ++i) CU(once());
+    for (int i = 0; i < iters; ++i)
+        if ((rc = once()) != MODEL_OK) return rc;
     CU(cudaEventRecord(b, st));
     CU(cudaEventSynchronize(b));
     float ms = 0.f;

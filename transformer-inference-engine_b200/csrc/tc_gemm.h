@@ -1,0 +1,54 @@
+// tc_gemm.h -- the tensor-core (tcgen05, 3xTF32) matmul's host interface.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace tie {
+
+// What the epilogue writes.
+enum TcOut : int {
+    TC_OUT_F32 = 0,       // C = y (fp32)
+    TC_OUT_HILO = 1,      // C_hi, C_lo = the tf32 split of y (input of the next matmul)
+    TC_OUT_F32_HILO = 2,  // both
+    TC_OUT_PARTIAL = 3    // raw partial sums of one K split (internal)
+};
+
+// A = a_hi + a_lo: M x K rows of lda floats; B = b_hi + b_lo: N x K rows of ldb.
+struct TcOperands {
+    const float* a_hi;
+    const float* a_lo;
+    int lda;
+    const float* b_hi;
+    const float* b_lo;
+    int ldb;
+};
+
+struct TcArgs {
+    int M, N, K;
+    int kb_per_split;        // filled in by the launcher
+    const float* bias;       // [N] (epilogues with bias)
+    float* C;                // [M, ldc] fp32 out (and the residual input)
+    float* C_hi;             // [M, ldc] tf32-split outputs
+    float* C_lo;
+    int ldc;
+    float* partial;          // split-K workspace: splits x M x N floats
+    int* err;                // device error flag (set when a bounded wait expires)
+};
+
+// hi = x rounded to tf32 (low 13 mantissa bits zero); x - hi is exact in fp32.
+__device__ __forceinline__ float tf32_hi(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+bool tc_gemm_supported(int M, int N, int K, int lda, int ldb);
+int tc_splits_for(int N, int K);
+cudaError_t launch_tc_gemm(const TcOperands& op, const TcArgs& a, int epi, int out, int splits,
+                           cudaStream_t st);
+// hi/lo = the tf32 split of x[0..n)
+cudaError_t launch_split_hilo(const float* x, float* hi, float* lo, long long n, cudaStream_t st);
+
+}  // namespace tie
