@@ -13,7 +13,33 @@ namespace tie {
 //   EPI_BIAS        y = acc + b                       (qkv += b, model.c:687-688)
 //   EPI_BIAS_GELU   y = gelu_new(acc + b)             (model.c:745-747, 615-623)
 //   EPI_BIAS_RESID  x = x + (acc + b), in place       (model.c:735-737, 750-752)
-enum Epi : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3 };
+//   EPI_QKV_KV      y = acc + b, and columns [E, 3E) also stored as this step's
+//                   K and V rows in the paged cache   (model.c:686-688, 822-824)
+enum Epi : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_BIAS_GELU = 2, EPI_BIAS_RESID = 3, EPI_QKV_KV = 4 };
+
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// while its predecessor is still running; it must call pdl_wait() before it
+// reads anything the predecessor writes, and calls pdl_trigger() once the
+// next kernel may be scheduled. Both are no-ops for a kernel launched without
+// the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // gelu_new with every product and sum rounded separately, in the reference's
 // evaluation order: inner = k * (x + ((0.044715 * x) * x) * x);
@@ -124,6 +150,16 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
                                int max_splits, float* part, float* out, AttnStats* stats,
                                cudaStream_t st, float* out_hi = nullptr, float* out_lo = nullptr,
                                int* counters = nullptr);
+
+// Small-batch (<= 16 rows) decode matmuls with optional LayerNorm prologue
+// (ln_g non-NULL) and PDL chaining (k_decode.cu).
+cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
+                            const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
+                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st);
+int dec_head_blocks(int V);
+cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
+                            const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
+                            int* part_idx, cudaStream_t st);
 
 // Step bookkeeping for device-resident greedy generation: tokens[b] = next[b];
 // out[b * ld + *step] = next[b]; lens[b] += 1; (block 0 thread 0) *step += 1.

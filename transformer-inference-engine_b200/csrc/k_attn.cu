@@ -339,6 +339,10 @@ attn_decode_combine_kernel(const int32_t* __restrict__ lens, int H, int max_spli
 // with an atomic -- merges all partials in chunk order (so the result does not
 // depend on which block was last) and resets the counter for the next launch.
 constexpr int KLD = D + 8;  // padded row: conflict-free 16-byte reads
+// chunk partials the merging block stages in shared memory: a 1024-position
+// context at chunk size CHT (longer contexts read the rest from global)
+template <int CHT>
+constexpr int merge_splits() { return 1024 / CHT; }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
@@ -346,20 +350,25 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
                  : "memory");
 }
 
+template <int CHT>
 __global__ void __launch_bounds__(128)
 attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int H, PagedKV kv,
                          int max_splits, float scale, float* __restrict__ part, int* __restrict__ counters,
                          float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo) {
     const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    pdl_trigger();
+    pdl_wait();
     const int ctx = lens[b] + 1;
-    const int ns = (ctx + CH - 1) / CH;
+    const int ns = (ctx + CHT - 1) / CHT;
     if (s >= ns) return;
-    const int p0 = s * CH, n = min(CH, ctx - p0);
+    const int p0 = s * CHT, n = min(CHT, ctx - p0);
     const int E = kv.n_embd;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ __align__(16) float Ks[CH * KLD];
-    __shared__ __align__(16) float Vs[CH * KLD];
-    __shared__ float s_e[CH];
+    __shared__ __align__(16) float Ks[CHT * KLD];
+    __shared__ __align__(16) float Vs[CHT * KLD];
+    constexpr int kMergeSplits = merge_splits<CHT>();
+    __shared__ float s_merge[kMergeSplits * PART];
+    __shared__ float s_e[CHT];
     __shared__ float s_red[8][D];
     __shared__ float s_w[4];
     __shared__ int s_last;
@@ -436,15 +445,21 @@ attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restric
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // the partials of this (sequence, head) into shared memory, all loads in
+    // flight together (beyond kMergeSplits of them, read from global)
+    const float* base = part + (size_t)(b * H + h) * max_splits * PART;
+    const int staged = min(ns, kMergeSplits);
+    for (int i = tid; i < staged * PART; i += 128) s_merge[i] = __ldcg(base + i);
+    __syncthreads();
+    auto P = [&](int i) { return i < staged * PART ? s_merge[i] : __ldcg(base + i); };
     if (tid < D) {
-        const float* base = part + (size_t)(b * H + h) * max_splits * PART;
-        float m = __ldcg(base);
-        for (int k = 1; k < ns; ++k) m = fmaxf(m, __ldcg(base + k * PART));
+        float m = P(0);
+        for (int k = 1; k < ns; ++k) m = fmaxf(m, P(k * PART));
         float lt = 0.f, o = 0.f;
         for (int k = 0; k < ns; ++k) {
-            const float c = expf(__ldcg(base + k * PART) - m);
-            lt = fmaf(__ldcg(base + k * PART + 1), c, lt);
-            o = fmaf(__ldcg(base + k * PART + 2 + tid), c, o);
+            const float c = expf(P(k * PART) - m);
+            lt = fmaf(P(k * PART + 1), c, lt);
+            o = fmaf(P(k * PART + 2 + tid), c, o);
         }
         const float y = o / lt;
         const size_t oi = (size_t)b * H * D + h * D + tid;
@@ -460,7 +475,8 @@ attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restric
 
 }  // namespace
 
-int attn_decode_max_splits(int capacity) { return (capacity + CH - 1) / CH; }
+// Partial-buffer sizing: the finest chunking any launch uses (16 positions).
+int attn_decode_max_splits(int capacity) { return (capacity + 15) / 16; }
 
 cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
                                 AttnStats* stats, cudaStream_t st, float* out_hi, float* out_lo) {
@@ -485,6 +501,7 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
                                cudaStream_t st, float* out_hi, float* out_lo, int* counters) {
     if (B <= 0) return cudaSuccess;
     const float scale = (float)(1.0 / sqrt((double)D));
+    if (stats || !counters) max_splits = (max_splits * 16 + CH - 1) / CH;  // 64-position chunks
     dim3 g1(max_splits, H, B), g2(H, B);
     if (stats) {
         float* e = part + (size_t)B * H * max_splits * PART;
@@ -492,8 +509,16 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
         attn_decode_split_kernel<true><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, e, e_ld);
         attn_decode_combine_kernel<true><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, out_hi, out_lo, e, e_ld, stats);
     } else if (counters) {
-        attn_decode_fused_kernel<<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, counters, out,
-                                                     out_hi, out_lo);
+        // 16-position chunks while the batch is small (more blocks in flight),
+        // 64-position chunks otherwise; `max_splits` is the sizing bound
+        const int capacity = max_splits * 16;
+        const bool fine = B <= 16;
+        const int splits = fine ? max_splits : (capacity + CH - 1) / CH;
+        cudaError_t e = fine ? launch_pdl(attn_decode_fused_kernel<16>, dim3(splits, H, B), dim3(128), 0, st, qkv,
+                                          lens, H, kv, splits, scale, part, counters, out, out_hi, out_lo)
+                             : launch_pdl(attn_decode_fused_kernel<CH>, dim3(splits, H, B), dim3(128), 0, st, qkv,
+                                          lens, H, kv, splits, scale, part, counters, out, out_hi, out_lo);
+        if (e != cudaSuccess) return e;
     } else {
         attn_decode_split_kernel<false><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, nullptr, 0);
         attn_decode_combine_kernel<false><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, out_hi, out_lo, nullptr, 0, nullptr);

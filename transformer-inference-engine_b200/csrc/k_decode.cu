@@ -1,0 +1,316 @@
+// k_decode.cu -- the small-batch decode step (at most 16 sequences), fused and
+// chained with programmatic dependent launch.
+//
+// A decode step at batch 1 moves ~0.5 GB of fp32 weights through a few dozen
+// matmuls whose individual transfers take ~1 us at HBM speed, so the step is
+// bound by the gaps between kernels as much as by bandwidth. Two measures:
+//
+//   * fusion: LayerNorm runs inside the matmul that consumes it (every block
+//     normalises the <= 16 input rows itself, in shared memory, with the same
+//     double-precision statistics as the standalone kernel), the K/V rows of a
+//     step are stored by the QKV matmul's epilogue, and LN_f runs inside the
+//     tied head;
+//   * programmatic dependent launch: every kernel first issues the loads of its
+//     own weight rows (which no earlier kernel writes), then lets the next
+//     kernel launch (griddepcontrol.launch_dependents), and only then waits for
+//     its predecessor's results (griddepcontrol.wait). Weight streaming thus
+//     overlaps the previous kernel's tail and the launch latency.
+//
+// Each warp holds all of its weight chunks in registers (loaded before the
+// dependency wait), so a matrix is in flight in one round trip.
+#include "common.cuh"
+
+namespace tie {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kMaxRows = 16;
+
+__device__ __forceinline__ float4 ld_stream(const float* p) {
+    float4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// LayerNorm of rows [0, M) of x (row stride ldx) into xs (row stride K), the
+// arithmetic of layernorm_kernel (k_misc.cu). Each row is first copied into
+// xs with all of the block's 16-byte loads in flight at once; the statistics
+// (one warp per row, double precision) and the normalisation then run out of
+// shared memory, in place.
+__device__ void ln_rows_to_smem(const float* __restrict__ x, int ldx, const float* __restrict__ g,
+                                const float* __restrict__ b, float eps, int M, int K, float* xs) {
+    const int K4 = K >> 2;
+    for (int i = threadIdx.x; i < M * K4; i += kWarps * 32) {
+        const int m = i / K4, c = i % K4;
+        reinterpret_cast<float4*>(xs + (size_t)m * K)[c] =
+            __ldg(reinterpret_cast<const float4*>(x + (size_t)m * ldx) + c);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = warp; m < M; m += kWarps) {
+        float* xr = xs + (size_t)m * K;
+        double s = 0.0;
+        for (int i = lane; i < K; i += 32) s = __dadd_rn(s, (double)xr[i]);
+        s = warp_sum_d(s);
+        const double mean = s / (double)K;
+        double v = 0.0;
+        for (int i = lane; i < K; i += 32) {
+            const double d = __dadd_rn((double)xr[i], -mean);
+            v = __dadd_rn(v, __dmul_rn(d, d));
+        }
+        v = warp_sum_d(v);
+        v = v / (double)K;
+        const float inv = (float)(1.0 / sqrt(__dadd_rn(v, (double)eps)));
+        for (int i = lane; i < K; i += 32) {
+            const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
+            xr[i] = __fadd_rn(__fmul_rn(nrm, g[i]), b[i]);
+        }
+    }
+}
+
+struct DecArgs {
+    const float* x;   // input rows [M][ldx] (pre-normalisation when LN)
+    int ldx;
+    const float* ln_g;
+    const float* ln_b;
+    float eps;
+    const float* W;   // [N][K], K-major
+    const float* bias;
+    float* y;         // [M][ldy]
+    int ldy;
+    int M, N, K;
+    // QKV epilogue: columns [E, 3E) are also this step's K and V rows
+    PagedKV kv;
+    const int32_t* lens;
+    // head: partial maxima per block
+    float* part_val;
+    int* part_idx;
+};
+
+enum : int { DEC_BIAS = 0, DEC_BIAS_GELU = 1, DEC_BIAS_RESID = 2, DEC_QKV_KV = 3, DEC_HEAD = 4 };
+
+__device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
+    return bi < 0 || v > bv || (v == bv && i < bi);
+}
+
+// A block of 4 warps covers RPB = (4 / WS) * RPW weight rows; each row's K is
+// cut into WS slices of K / WS and each warp owns RPW rows of one slice. A warp
+// loads ALL of its weight chunks (at most CPL 16-byte chunks per lane per row)
+// into registers before the dependency wait, so the whole matrix is in flight
+// at once; after the wait it only reads the <= 16 activation rows (shared
+// memory when normalised here, else global through L1) and reduces.
+// Per (row, activation row) the sum is: within a slice, lane c accumulates
+// chunks c, c + 32, ... (four FMAs per chunk, in order), then an xor-butterfly
+// across lanes; the WS slice sums are added in slice order. The order depends
+// only on K, so results do not depend on the batch a sequence decodes in.
+template <int EPI, bool LN, int RPW, int WS, int CPL>
+__global__ void __launch_bounds__(kWarps * 32)
+dec_gemv_kernel(DecArgs a) {
+    extern __shared__ __align__(16) float xs[];  // [M][K] when LN
+    constexpr int GROUPS = kWarps / WS;          // row groups per block
+    __shared__ float s_part[GROUPS][WS][RPW][kMaxRows];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = warp / WS, ks = warp % WS;
+    const int row0 = (blockIdx.x * GROUPS + grp) * RPW;
+    const int K4 = a.K >> 2;
+    const int slice = (K4 + WS - 1) / WS;          // 16-byte chunks per slice
+    const int c0 = ks * slice, c1 = min(K4, c0 + slice);
+
+    // 1. every weight chunk of this warp, before the dependency wait
+    float4 w[RPW][CPL];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int u = 0; u < CPL; ++u) {
+            const int c = c0 + u * 32 + lane;
+            w[r][u] = (row0 + r < a.N && c < c1) ? ld_stream(a.W + (size_t)(row0 + r) * a.K + 4 * c)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    pdl_trigger();
+    pdl_wait();
+
+    // 2. the activation rows
+    const float* X = a.x;
+    int ldx = a.ldx;
+    if constexpr (LN) {
+        ln_rows_to_smem(a.x, a.ldx, a.ln_g, a.ln_b, a.eps, a.M, a.K, xs);
+        __syncthreads();
+        X = xs;
+        ldx = a.K;
+    }
+
+    // 3. slice sums
+    float acc[RPW][kMaxRows];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < kMaxRows; ++m) acc[r][m] = 0.f;
+#pragma unroll
+    for (int u = 0; u < CPL; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < c1) {
+#pragma unroll
+            for (int m = 0; m < kMaxRows; ++m) {
+                if (m < a.M) {
+                    const float4 xv = LN ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
+                                         : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        float t = acc[r][m];
+                        t = fmaf(w[r][u].x, xv.x, t);
+                        t = fmaf(w[r][u].y, xv.y, t);
+                        t = fmaf(w[r][u].z, xv.z, t);
+                        t = fmaf(w[r][u].w, xv.w, t);
+                        acc[r][m] = t;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < kMaxRows; ++m) {
+            if (m >= a.M) break;  // uniform across the block
+            float v = acc[r][m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            acc[r][m] = v;
+        }
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < kMaxRows; ++m) s_part[grp][ks][r][m] = acc[r][m];
+    }
+    __syncthreads();
+
+    // 4. epilogue: slice sums in slice order; thread t of a row group handles
+    //    (row r, activation row m) pairs
+    if constexpr (EPI != DEC_HEAD) {
+        const int t = threadIdx.x % (WS * 32);
+        if (warp % WS == 0 || WS == 1) {
+            for (int q = (WS == 1 ? lane : t); q < RPW * a.M; q += (WS == 1 ? 32 : WS * 32)) {
+                const int r = q / a.M, m = q % a.M;
+                const int j = row0 + r;
+                if (j >= a.N) continue;
+                float sum = s_part[grp][0][r][m];
+#pragma unroll
+                for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
+                float* yp = a.y + (size_t)m * a.ldy + j;
+                float v;
+                if constexpr (EPI == DEC_BIAS || EPI == DEC_QKV_KV) v = apply_epi<EPI_BIAS>(sum, a.bias, j, yp);
+                else if constexpr (EPI == DEC_BIAS_GELU) v = apply_epi<EPI_BIAS_GELU>(sum, a.bias, j, yp);
+                else v = apply_epi<EPI_BIAS_RESID>(sum, a.bias, j, yp);
+                *yp = v;
+                if constexpr (EPI == DEC_QKV_KV) {
+                    const int E = a.kv.n_embd;
+                    if (j >= E) {
+                        const size_t row = a.kv.row(m, a.lens[m]);
+                        if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
+                        else a.kv.v[row * E + (j - 2 * E)] = v;
+                    }
+                }
+            }
+        }
+    } else {
+        // logits (optional) and this block's best (value, index) per activation
+        // row; NaN at index 0 is reported as index -2 (the reference's scan never
+        // leaves index 0 then)
+        if ((int)threadIdx.x < a.M) {
+            const int m = threadIdx.x;
+            float bv = 0.f;
+            int bi = -1;
+            bool nan0 = false;
+            for (int g = 0; g < GROUPS; ++g)
+                for (int r = 0; r < RPW; ++r) {
+                    const int j = (blockIdx.x * GROUPS + g) * RPW + r;
+                    if (j >= a.N) continue;
+                    float v = s_part[g][0][r][m];
+                    for (int k = 1; k < WS; ++k) v += s_part[g][k][r][m];
+                    if (a.y) a.y[(size_t)m * a.ldy + j] = v;
+                    if (j == 0 && !(v == v)) nan0 = true;
+                    else if (v == v && beats(v, j, bv, bi)) { bv = v; bi = j; }
+                }
+            a.part_val[(size_t)blockIdx.x * a.M + m] = bv;
+            a.part_idx[(size_t)blockIdx.x * a.M + m] = nan0 ? -2 : bi;
+        }
+    }
+}
+
+template <int EPI, bool LN, int RPW, int WS, int CPL>
+cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
+    const size_t smem = LN ? (size_t)a.M * a.K * sizeof(float) : 0;
+    auto k = dec_gemv_kernel<EPI, LN, RPW, WS, CPL>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    constexpr int rows_per_block = (kWarps / WS) * RPW;
+    const int grid = (a.N + rows_per_block - 1) / rows_per_block;
+    cudaError_t e = launch_pdl(k, dim3(grid), dim3(kWarps * 32), smem, st, a);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// The slicing of K for a matrix: each lane holds at most 8 chunks per row.
+//   K <= 1024 (K4 <= 256): whole rows, WS = 1
+//   K <= 4096: WS = 4; K <= 8192: WS = 4 with 16 chunks per lane
+template <int EPI, bool LN>
+cudaError_t dec_dispatch(const DecArgs& a, cudaStream_t st) {
+    const int K4 = a.K >> 2;
+    if (K4 <= 256) return dec_launch<EPI, LN, 1, 1, 8>(a, st);
+    if (K4 <= 1024) return dec_launch<EPI, LN, 1, 4, 8>(a, st);
+    if (K4 <= 2048) return dec_launch<EPI, LN, 1, 4, 16>(a, st);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int dec_head_blocks(int V) { return (V + kWarps * 4 - 1) / (kWarps * 4); }  // RPW 4, WS 1
+
+// y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL.
+cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
+                            const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
+                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st) {
+    if (M <= 0 || M > kMaxRows || (K & 3) || (ldx & 3)) return cudaErrorInvalidValue;
+    DecArgs a{};
+    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W; a.bias = bias;
+    a.y = y; a.ldy = ldy; a.M = M; a.N = N; a.K = K;
+    if (kv) a.kv = *kv;
+    a.lens = lens;
+    const bool ln = ln_g != nullptr;
+    switch (epi) {
+        case EPI_BIAS: return ln ? dec_dispatch<DEC_BIAS, true>(a, st) : dec_dispatch<DEC_BIAS, false>(a, st);
+        case EPI_BIAS_GELU:
+            return ln ? dec_dispatch<DEC_BIAS_GELU, true>(a, st) : dec_dispatch<DEC_BIAS_GELU, false>(a, st);
+        case EPI_BIAS_RESID:
+            return ln ? dec_dispatch<DEC_BIAS_RESID, true>(a, st) : dec_dispatch<DEC_BIAS_RESID, false>(a, st);
+        case EPI_QKV_KV:
+            if (!kv || !lens) return cudaErrorInvalidValue;
+            return ln ? dec_dispatch<DEC_QKV_KV, true>(a, st) : dec_dispatch<DEC_QKV_KV, false>(a, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+// The tied head with LN_f in its prologue: logits (optional) and per-block
+// partial maxima for launch_argmax_finalize.
+cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
+                            const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
+                            int* part_idx, cudaStream_t st) {
+    if (M <= 0 || M > kMaxRows || (K & 3) || (ldx & 3)) return cudaErrorInvalidValue;
+    DecArgs a{};
+    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W;
+    a.y = logits; a.ldy = ldl; a.M = M; a.N = V; a.K = K; a.part_val = part_val; a.part_idx = part_idx;
+    if ((K >> 2) > 256) return cudaErrorInvalidValue;  // the head's K is n_embd
+    return ln_g ? dec_launch<DEC_HEAD, true, 4, 1, 8>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8>(a, st);
+}
+
+}  // namespace tie

@@ -47,6 +47,8 @@ __global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
                                     const int32_t* __restrict__ lens, int B,
                                     const float* __restrict__ wte,
                                     const float* __restrict__ wpe, float* __restrict__ x, int E, int V) {
+    pdl_trigger();
+    pdl_wait();
     const int E4 = E >> 2;
     const int n = B * E4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -67,15 +69,26 @@ __global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
 // ------------------------------------------------------------- LayerNorm --
 // model.c:593-610: mean and biased variance in double, inv = (float)(1/sqrt(var
 // + eps)), normalized = (float)((x - mean) * inv), then a float multiply by the
-// gain and a float add of the shift, each rounded separately. One warp per row.
-__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
-                                 const float* __restrict__ bvec, float* __restrict__ y,
-                                 float* __restrict__ y_hi, float* __restrict__ y_lo,
-                                 int rows, int E, float eps) {
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+// gain and a float add of the shift, each rounded separately. One warp per row;
+// the row is first staged in shared memory with all its 16-byte loads in
+// flight, so the statistics do not wait on one load at a time.
+constexpr int kLnWarps = 4;
+constexpr int kLnMaxK = 2048;
+
+__global__ void __launch_bounds__(kLnWarps * 32)
+layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                 const float* __restrict__ bvec, float* __restrict__ y,
+                 float* __restrict__ y_hi, float* __restrict__ y_lo,
+                 int rows, int E, float eps) {
+    __shared__ __align__(16) float rs[kLnWarps][kLnMaxK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kLnWarps + warp;
     if (row >= rows) return;
-    const float* xr = x + (size_t)row * E;
+    float* xr = rs[warp];
+    const int E4 = E >> 2;
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * E);
+    for (int c = lane; c < E4; c += 32) reinterpret_cast<float4*>(xr)[c] = src[c];
+    __syncwarp();
     double s = 0.0;
     for (int i = lane; i < E; i += 32) s = __dadd_rn(s, (double)xr[i]);
     s = warp_sum_d(s);
@@ -91,12 +104,12 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
     const size_t off = (size_t)row * E;
     for (int i = lane; i < E; i += 32) {
         const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
-        const float v = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
-        if (y) y[off + i] = v;
+        const float val = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
+        if (y) y[off + i] = val;
         if (y_hi) {
-            const float h = tf32_hi(v);
+            const float h = tf32_hi(val);
             y_hi[off + i] = h;
-            y_lo[off + i] = __fsub_rn(v, h);
+            y_lo[off + i] = __fsub_rn(val, h);
         }
     }
 }
@@ -144,16 +157,28 @@ __device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
 
 __global__ void argmax_finalize_kernel(const float* __restrict__ pv, const int* __restrict__ pi,
                                        int n_parts, int M, int32_t* __restrict__ next) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     if (m >= M) return;
     float bv = 0.f;
     int bi = -1;
     bool nan0 = false;
-    for (int p = threadIdx.x; p < n_parts; p += blockDim.x) {
-        const int i = pi[(size_t)p * M + m];
-        const float v = pv[(size_t)p * M + m];
-        if (i == -2) nan0 = true;
-        else if (i >= 0 && beats(v, i, bv, bi)) { bv = v; bi = i; }
+    // 8 partials per thread per round, all loaded before any is compared
+    for (int p0 = threadIdx.x; p0 < n_parts; p0 += 8 * blockDim.x) {
+        int ii[8];
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int p = p0 + u * blockDim.x;
+            ii[u] = p < n_parts ? pi[(size_t)p * M + m] : -1;
+            vv[u] = p < n_parts ? pv[(size_t)p * M + m] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (ii[u] == -2) nan0 = true;
+            else if (ii[u] >= 0 && beats(vv[u], ii[u], bv, bi)) { bv = vv[u]; bi = ii[u]; }
+        }
     }
     __shared__ float sv[32];
     __shared__ int si[32];
@@ -211,6 +236,8 @@ __global__ void argmax_rows_kernel(const float* __restrict__ L, int ldl, int N, 
 __global__ void step_advance_kernel(const int32_t* __restrict__ next, int32_t* __restrict__ tokens,
                                     int32_t* __restrict__ lens, int32_t* __restrict__ out,
                                     int ld_out, int32_t* __restrict__ step, int B) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     const int s = *step;
     __syncthreads();
@@ -284,9 +311,9 @@ cudaError_t launch_embed_decode(const int32_t* tokens, const int32_t* lens, int 
 
 cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float* y, int rows,
                              int E, float eps, cudaStream_t st, float* y_hi, float* y_lo) {
-    const int warps_per_block = 8;
-    const int grid = (rows + warps_per_block - 1) / warps_per_block;
-    layernorm_kernel<<<grid, warps_per_block * 32, 0, st>>>(x, g, b, y, y_hi, y_lo, rows, E, eps);
+    if (E > kLnMaxK || (E & 3)) return cudaErrorInvalidValue;
+    const int grid = (rows + kLnWarps - 1) / kLnWarps;
+    layernorm_kernel<<<grid, kLnWarps * 32, 0, st>>>(x, g, b, y, y_hi, y_lo, rows, E, eps);
     return cudaGetLastError();
 }
 
@@ -306,8 +333,8 @@ cudaError_t launch_kv_store_decode(const float* qkv, const int32_t* lens, int B,
 
 cudaError_t launch_argmax_finalize(const float* part_val, const int* part_idx, int n_parts, int M,
                                    int32_t* next, cudaStream_t st) {
-    argmax_finalize_kernel<<<M, 256, 0, st>>>(part_val, part_idx, n_parts, M, next);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(argmax_finalize_kernel, dim3(M), dim3(256), 0, st, part_val, part_idx, n_parts, M, next);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_argmax_rows(const float* L, int ldl, int M, int N, int row_stride,
@@ -320,8 +347,8 @@ cudaError_t launch_step_advance(const int32_t* next, int32_t* tokens, int32_t* l
                                 int32_t* out, int ld_out, int32_t* step, int B, cudaStream_t st) {
     // One block: every thread reads *step before thread 0 advances it.
     if (B > 1024) return cudaErrorInvalidValue;
-    step_advance_kernel<<<1, 1024, 0, st>>>(next, tokens, lens, out, ld_out, step, B);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(step_advance_kernel, dim3(1), dim3(1024), 0, st, next, tokens, lens, out, ld_out, step, B);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_transpose(const float* in, float* out, int R, int Cc, cudaStream_t st) {

@@ -35,7 +35,7 @@
 namespace tie {
 namespace {
 
-constexpr int BM = 128, BK = 32;
+constexpr int BM = 128, BK = 16;
 constexpr int THREADS = 192;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -90,13 +90,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 bytes
-// in 8-row (1024-byte) groups. Start address and strides in 16-byte units.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+// Shared-memory matrix descriptor: K-major, 64-byte swizzle (SWIZZLE_64B,
+// layout code 4): rows of 64 bytes (16 tf32) in 8-row, 512-byte groups. Start
+// address and strides in 16-byte units; the leading offset is unused for a
+// swizzled K-major layout.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
     const uint64_t start = (addr >> 4) & 0x3FFFu;
-    const uint64_t lbo = 1;          // unused for swizzled K-major
-    const uint64_t sbo = 1024 >> 4;  // between 8-row groups
-    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (2ull << 61) /* SW128 */;
+    const uint64_t lbo = 1;
+    const uint64_t sbo = 512 >> 4;
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (4ull << 61) /* SW64 */;
 }
 
 // kind::tf32 instruction descriptor: fp32 accumulate, tf32 A and B, both
@@ -120,6 +122,10 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                  : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -134,49 +140,60 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// One pipeline stage: A hi/lo (BM x BK) and B hi/lo (BN x BK), 64-byte rows.
 template <int BN>
-constexpr size_t stage_bytes() { return 2 * (size_t)BM * 128 + 2 * (size_t)BN * 128; }
+constexpr uint32_t stage_bytes() { return 2u * BM * 64 + 2u * BN * 64; }
 
 template <int BN>
-constexpr int stages() { return BN >= 256 ? 2 : 3; }
+constexpr int stages() { return (int)((192u * 1024) / stage_bytes<BN>()); }
 
 template <int BN>
 constexpr size_t smem_bytes() {
-    return 1024 /* alignment slack */ + stages<BN>() * stage_bytes<BN>() + 256 /* barriers */;
+    return 1024 /* alignment slack */ + (size_t)stages<BN>() * stage_bytes<BN>() + 256 /* barriers */;
 }
 
+// Persistent, warp-specialised: each block loops over output tiles
+// (blockIdx.x, + gridDim.x, ...). The TMEM accumulator is double-buffered, so
+// the epilogue warps drain tile i while the MMA warp accumulates tile i + 1.
 template <int BN, int EPI, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                TcArgs p) {
     constexpr int S = stages<BN>();
-    constexpr uint32_t kStageBytes = (uint32_t)stage_bytes<BN>();
-    constexpr uint32_t kTileA = BM * 128, kTileB = BN * 128;
+    constexpr uint32_t kStage = stage_bytes<BN>();
+    constexpr uint32_t kTileA = BM * 64, kTileB = BN * 64;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
-    uint64_t* full = bars;            // [S]
-    uint64_t* empty = bars + S;       // [S]
-    uint64_t* accum = bars + 2 * S;   // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage);
+    uint64_t* full = bars;              // [S]   TMA -> MMA
+    uint64_t* empty = bars + S;         // [S]   MMA -> TMA
+    uint64_t* tfull = bars + 2 * S;     // [2]   MMA -> epilogue
+    uint64_t* tempty = bars + 2 * S + 2;  // [2] epilogue -> MMA
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-    const int kb0 = blockIdx.z * p.kb_per_split;
-    const int nkb = min(p.kb_per_split, p.K / BK - kb0);
+    const int tiles_n = (p.N + BN - 1) / BN, tiles_m = (p.M + BM - 1) / BM;
+    const int tiles_mn = tiles_n * tiles_m;
+    const int n_tiles = tiles_mn * p.splits;
+    const int kb_total = p.K / BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 1);
         }
-        mbar_init(smem_u32(accum), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tfull[b]), 1);
+            mbar_init(smem_u32(&tempty[b]), 4);  // one arrival per epilogue warp
+        }
+        *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)BN));
+                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)(2 * BN)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -184,91 +201,170 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = *tmem_slot;
 
+    auto tile_k_range = [&](int z, int& kb0, int& nkb) {
+        kb0 = z * p.kb_per_split;
+        nkb = min(p.kb_per_split, kb_total - kb0);
+    };
+    auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (mbar_try_wait(bar, parity)) return true;
+            if ((i & 255u) == 0) {
+                if (*abort_flag) return false;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
+        }
+        *abort_flag = 1;
+        atomicExch(p.err, 1);
+        return false;
+    };
+
     if (warp == 0) {
         // ------------------------------------------------------- producer
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S;
-                const uint32_t ph = (uint32_t)((kb / S) & 1);
-                if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) break;
-                const uint32_t base = smem_u32(smem + s * kStageBytes);
-                const uint32_t fb = smem_u32(&full[s]);
-                mbar_expect_tx(fb, kStageBytes);
-                const int kx = (kb0 + kb) * BK;
-                tma_load_2d(base, &ta_hi, fb, kx, m0);
-                tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
-                tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
-                tma_load_2d(base + 2 * kTileA + kTileB, &tb_lo, fb, kx, n0);
-                ++issued;
+            uint32_t it = 0;  // k-blocks issued so far (ring position)
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+                const int z = t / tiles_mn, r = t % tiles_mn;
+                const int m0 = (r / tiles_n) * BM, n0 = (r % tiles_n) * BN;
+                int kb0, nkb;
+                tile_k_range(z, kb0, nkb);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!wait(smem_u32(&empty[s]), ((it / S) & 1u) ^ 1u)) { ok = false; break; }
+                    const uint32_t base = smem_u32(smem + s * kStage);
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_expect_tx(fb, kStage);
+                    const int kx = (kb0 + kb) * BK;
+                    tma_load_2d(base, &ta_hi, fb, kx, m0);
+                    tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
+                    tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
+                    tma_load_2d(base + 2 * kTileA + kTileB, &tb_lo, fb, kx, n0);
+                }
             }
             // drain: every copy this thread started has landed before exit
-            for (int kb = max(0, issued - S); kb < issued; ++kb)
-                mbar_wait(smem_u32(&full[kb % S]), (uint32_t)((kb / S) & 1), p.err);
+            for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it; ++j) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(&full[j % S]), (j / S) & 1u))
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) { atomicExch(p.err, 1); break; }
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32<BN>();
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S;
-                if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((kb / S) & 1), p.err)) break;
+            uint32_t it = 0;
+            int i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++i) {
+                const int buf = i & 1;
+                const uint32_t use = (uint32_t)(i >> 1);
+                if (!wait(smem_u32(&tempty[buf]), (use & 1u) ^ 1u)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t base = smem_u32(smem + s * kStageBytes);
+                const uint32_t acc = tmem + (uint32_t)(buf * BN);
+                int kb0, nkb;
+                tile_k_range(t / tiles_mn, kb0, nkb);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!wait(smem_u32(&full[s]), (it / S) & 1u)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint32_t base = smem_u32(smem + s * kStage);
 #pragma unroll
-                for (int j = 0; j < BK / 8; ++j) {  // 4 k-steps of 8 tf32 (32 bytes) each
-                    const uint64_t a_hi = sw128_desc(base + j * 32);
-                    const uint64_t a_lo = sw128_desc(base + kTileA + j * 32);
-                    const uint64_t b_hi = sw128_desc(base + 2 * kTileA + j * 32);
-                    const uint64_t b_lo = sw128_desc(base + 2 * kTileA + kTileB + j * 32);
-                    mma_tf32(tmem, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-                    mma_tf32(tmem, a_hi, b_lo, idesc, 1u);
-                    mma_tf32(tmem, a_hi, b_hi, idesc, 1u);
+                    for (int j = 0; j < BK / 8; ++j) {  // k-steps of 8 tf32 (32 bytes)
+                        const uint64_t a_hi = sw64_desc(base + j * 32);
+                        const uint64_t a_lo = sw64_desc(base + kTileA + j * 32);
+                        const uint64_t b_hi = sw64_desc(base + 2 * kTileA + j * 32);
+                        const uint64_t b_lo = sw64_desc(base + 2 * kTileA + kTileB + j * 32);
+                        mma_tf32(acc, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                        mma_tf32(acc, a_hi, b_lo, idesc, 1u);
+                        mma_tf32(acc, a_hi, b_hi, idesc, 1u);
+                    }
+                    mma_commit(smem_u32(&empty[s]));
                 }
-                mma_commit(smem_u32(&empty[s]));
+                // arrives once this tile's MMAs have completed (also when cut short)
+                mma_commit(smem_u32(&tfull[buf]));
             }
-            // arrives once every MMA issued above has completed (also on the error path)
-            mma_commit(smem_u32(accum));
         }
     } else {
         // ------------------------------------------------------- epilogue
         const int q = warp & 3;  // this warp's TMEM lane quarter
-        const bool ok = mbar_wait(smem_u32(accum), 0u, p.err) && nkb > 0;
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const int row = m0 + q * 32 + lane;
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            const int buf = i & 1;
+            const uint32_t use = (uint32_t)(i >> 1);
+            const int z = t / tiles_mn, r = t % tiles_mn;
+            const int m0 = (r / tiles_n) * BM, n0 = (r % tiles_n) * BN;
+            const bool ok = wait(smem_u32(&tfull[buf]), use & 1u);
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
-            if (!ok || row >= p.M) continue;
-            const int col0 = n0 + c * 32;
-            if constexpr (OUT == TC_OUT_PARTIAL) {
-                float* dst = p.partial + ((size_t)blockIdx.z * p.M + row) * p.N + col0;
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), v);
+                if (!ok || row >= p.M) continue;
+                const int col0 = n0 + c * 32;
+                const bool full_chunk = col0 + 32 <= p.N;
+                if constexpr (OUT == TC_OUT_PARTIAL) {
+                    float* dst = p.partial + ((size_t)z * p.M + row) * p.N + col0;
+                    if (full_chunk && (p.N & 3) == 0) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (col0 + i < p.N) dst[i] = __uint_as_float(r[i]);
-            } else {
+                        for (int i4 = 0; i4 < 8; ++i4)
+                            reinterpret_cast<float4*>(dst)[i4] =
+                                make_float4(__uint_as_float(v[4 * i4]), __uint_as_float(v[4 * i4 + 1]),
+                                            __uint_as_float(v[4 * i4 + 2]), __uint_as_float(v[4 * i4 + 3]));
+                    } else {
+                        for (int k = 0; k < 32; ++k)
+                            if (col0 + k < p.N) dst[k] = __uint_as_float(v[k]);
+                    }
+                } else {
+                    const size_t o = (size_t)row * p.ldc + col0;
+                    float y[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = col0 + i;
-                    if (col >= p.N) continue;
-                    const size_t o = (size_t)row * p.ldc + col;
-                    const float y = apply_epi<EPI>(__uint_as_float(r[i]), p.bias, col, p.C + o);
-                    if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o] = y;
-                    if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
-                        const float hi = tf32_hi(y);
-                        p.C_hi[o] = hi;
-                        p.C_lo[o] = __fsub_rn(y, hi);
+                    for (int k = 0; k < 32; ++k)
+                        y[k] = (col0 + k < p.N) ? apply_epi<EPI>(__uint_as_float(v[k]), p.bias, col0 + k, p.C + o + k)
+                                                : 0.f;
+                    if (full_chunk && (p.ldc & 3) == 0) {
+#pragma unroll
+                        for (int i4 = 0; i4 < 8; ++i4) {
+                            if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO)
+                                reinterpret_cast<float4*>(p.C + o)[i4] =
+                                    make_float4(y[4 * i4], y[4 * i4 + 1], y[4 * i4 + 2], y[4 * i4 + 3]);
+                            if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
+                                float h[4], l[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    h[e] = tf32_hi(y[4 * i4 + e]);
+                                    l[e] = __fsub_rn(y[4 * i4 + e], h[e]);
+                                }
+                                reinterpret_cast<float4*>(p.C_hi + o)[i4] = make_float4(h[0], h[1], h[2], h[3]);
+                                reinterpret_cast<float4*>(p.C_lo + o)[i4] = make_float4(l[0], l[1], l[2], l[3]);
+                            }
+                        }
+                    } else {
+                        for (int k = 0; k < 32; ++k) {
+                            if (col0 + k >= p.N) break;
+                            if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o + k] = y[k];
+                            if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
+                                const float h = tf32_hi(y[k]);
+                                p.C_hi[o + k] = h;
+                                p.C_lo[o + k] = __fsub_rn(y[k], h);
+                            }
+                        }
                     }
                 }
             }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[buf]));
+            if (!ok) break;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)));
     }
 }
 
@@ -318,7 +414,8 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D map over a rows x cols fp32 matrix (row stride ld floats), box 32 x box_rows.
+// 2-D map over a rows x cols fp32 matrix (row stride ld floats), box BK x box_rows,
+// 64-byte swizzle (the layout sw64_desc describes).
 bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
@@ -327,8 +424,18 @@ bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, i
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    }
+    return n;
 }
 
 template <int BN, int EPI, int OUT>
@@ -341,8 +448,10 @@ cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStr
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, OUT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM, splits);
-    tc_gemm_kernel<BN, EPI, OUT><<<grid, THREADS, smem, st>>>(m[0], m[1], m[2], m[3], a);
+    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM) * splits;
+    TcArgs b = a;
+    b.splits = splits;
+    tc_gemm_kernel<BN, EPI, OUT><<<std::min(tiles, num_sms()), THREADS, smem, st>>>(m[0], m[1], m[2], m[3], b);
     return cudaGetLastError();
 }
 

@@ -471,6 +471,30 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
     const Mat ff{m->ff, m->ff_hi, m->ff_lo};
     model_status rc;
     LAUNCH(launch_embed_decode(m->d_tokens, m->d_lens, B, m->wte, m->wpe, m->x, E, V, st));
+    if (small) {
+        // fused, PDL-chained kernels: 5 per layer (k_decode.cu)
+        for (int l = 0; l < m->cfg.n_layer; ++l) {
+            const Layer& w = m->layers[l];
+            const PagedKV view = layer_view(cache, l);
+            LAUNCH(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, eps, w.qkv_w, w.qkv_b, m->qkv, 3 * E, B, 3 * E, E,
+                                   EPI_QKV_KV, &view, m->d_lens, st));
+            LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st,
+                                      nullptr, nullptr, m->d_attn_cnt));
+            if (stats) ++m->launches;  // the separate merge kernel
+            LAUNCH(launch_dec_gemv(m->attn, E, nullptr, nullptr, eps, w.proj_w, w.proj_b, m->x, E, B, E, E,
+                                   EPI_BIAS_RESID, nullptr, nullptr, st));
+            LAUNCH(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, eps, w.fc_w, w.fc_b, m->ff, 4 * E, B, 4 * E, E,
+                                   EPI_BIAS_GELU, nullptr, nullptr, st));
+            LAUNCH(launch_dec_gemv(m->ff, 4 * E, nullptr, nullptr, eps, w.mlp_w, w.mlp_b, m->x, E, B, E, 4 * E,
+                                   EPI_BIAS_RESID, nullptr, nullptr, st));
+        }
+        LAUNCH(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
+                               m->d_am_idx, st));
+        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V), B, m->d_next, st));
+        if (advance)
+            LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
+        return MODEL_OK;
+    }
     for (int l = 0; l < m->cfg.n_layer; ++l) {
         const Layer& w = m->layers[l];
         const PagedKV view = layer_view(cache, l);
@@ -479,32 +503,25 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
                          m->qkv, nullptr, nullptr, 3 * E)) != MODEL_OK)
             return rc;
         LAUNCH(launch_kv_store_decode(m->qkv, m->d_lens, B, view, st));
-        LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part,
-                                  small ? m->attn : nullptr, stats, st, small ? nullptr : m->attn_hi,
-                                  small ? nullptr : m->attn_lo, m->d_attn_cnt));
+        LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, nullptr, stats, st,
+                                  m->attn_hi, m->attn_lo, m->d_attn_cnt));
         if (stats) ++m->launches;  // the separate merge kernel
         if ((rc = matmul(m, true, B, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
                          EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
             return rc;
         LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, xb_f, B, E, eps, st, xb_h, xb_l));
         if ((rc = matmul(m, true, B, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
-                         small ? m->ff : nullptr, small ? nullptr : m->ff_hi, small ? nullptr : m->ff_lo,
-                         4 * E)) != MODEL_OK)
+                         nullptr, m->ff_hi, m->ff_lo, 4 * E)) != MODEL_OK)
             return rc;
         if ((rc = matmul(m, true, B, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
                          EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
             return rc;
     }
     LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, xb_f, B, E, eps, st, xb_h, xb_l));
-    if (small) {
-        LAUNCH(launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val, m->d_am_idx, st));
-        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, gemv_argmax_blocks(V), B, m->d_next, st));
-    } else {
-        if ((rc = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr, EPI_STORE,
-                         m->logits, nullptr, nullptr, V)) != MODEL_OK)
-            return rc;
-        LAUNCH(launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st));
-    }
+    if ((rc = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr, EPI_STORE,
+                     m->logits, nullptr, nullptr, V)) != MODEL_OK)
+        return rc;
+    LAUNCH(launch_argmax_rows(m->logits, V, B, V, 1, 0, m->d_next, st));
     if (advance) LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
     return MODEL_OK;
 }
@@ -1235,6 +1252,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
     if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
     const size_t R = kernel >= TIE_KERNEL_PREFILL_ATTENTION ? rows * context : rows;
     CU(cudaMemsetAsync(m->qkv, 0, R * 3 * E * sizeof(float), st));
+    CU(cudaMemsetAsync(m->x, 0, R * E * sizeof(float), st));
     CU(cudaMemsetAsync(m->xb, 0, R * E * sizeof(float), st));
     CU(cudaMemsetAsync(m->ff, 0, R * 4 * E * sizeof(float), st));
     const Layer& w = m->layers[0];
@@ -1253,19 +1271,34 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                                       m->d_attn_cnt));
                 return MODEL_OK;
             case TIE_KERNEL_DECODE_QKV:
+                if (small) {
+                    CU(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, m->cfg.layer_norm_epsilon, w.qkv_w, w.qkv_b, m->qkv,
+                                       3 * E, B, 3 * E, E, EPI_QKV_KV, &view, m->d_lens, st));
+                    return MODEL_OK;
+                }
                 return matmul(m, true, B, xb, E, Mat{w.qkv_w, w.qkv_hi, w.qkv_lo}, 3 * E, E, w.qkv_b, EPI_BIAS,
                               m->qkv, nullptr, nullptr, 3 * E);
             case TIE_KERNEL_DECODE_FC:
+                if (small) {
+                    CU(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, m->cfg.layer_norm_epsilon, w.fc_w, w.fc_b, m->ff,
+                                       4 * E, B, 4 * E, E, EPI_BIAS_GELU, nullptr, nullptr, st));
+                    return MODEL_OK;
+                }
                 return matmul(m, true, B, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
-                              small ? m->ff : nullptr, small ? nullptr : m->ff_hi, small ? nullptr : m->ff_lo,
-                              4 * E);
+                              nullptr, m->ff_hi, m->ff_lo, 4 * E);
             case TIE_KERNEL_DECODE_MLP_PROJ:
+                if (small) {
+                    CU(launch_dec_gemv(m->ff, 4 * E, nullptr, nullptr, 0.f, w.mlp_w, w.mlp_b, m->x, E, B, E, 4 * E,
+                                       EPI_BIAS_RESID, nullptr, nullptr, st));
+                    return MODEL_OK;
+                }
                 return matmul(m, true, B, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
                               EPI_BIAS_RESID, m->x, nullptr, nullptr, E);
             case TIE_KERNEL_DECODE_HEAD:
                 if (small) {
-                    CU(launch_gemv_argmax(m->xb, E, m->wte, E, m->logits, V, B, V, E, m->d_am_val, m->d_am_idx, st));
-                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, gemv_argmax_blocks(V), B, m->d_next, st));
+                    CU(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, m->cfg.layer_norm_epsilon, m->wte, m->logits, V,
+                                       B, V, E, m->d_am_val, m->d_am_idx, st));
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V), B, m->d_next, st));
                     return MODEL_OK;
                 } else {
                     model_status r = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr,

@@ -28,6 +28,7 @@ struct TcOperands {
 struct TcArgs {
     int M, N, K;
     int kb_per_split;        // filled in by the launcher
+    int splits;              // filled in by the launcher
     const float* bias;       // [N] (epilogues with bias)
     float* C;                // [M, ldc] fp32 out (and the residual input)
     float* C_hi;             // [M, ldc] tf32-split outputs
