@@ -203,6 +203,10 @@ def run_reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------- our arm --
+# decode steps of at most this many sequences run as one persistent kernel
+STEP_ROWS = 4
+
+
 def roofline_of(m, wl, rows, measured, peaks):
     """Per-kernel live timings (CUDA events, each kernel alone at the workload's
     shapes) and the roofline of the dominant one."""
@@ -225,7 +229,12 @@ def roofline_of(m, wl, rows, measured, peaks):
         k[name]["share_ms"] = ms * per_step
         k[name]["work_per_launch"] = work
 
-    if steps > 0:
+    if steps > 0 and rows <= STEP_ROWS:
+        # the persistent step kernel: every weight matrix once, the KV cache of
+        # every layer once, per step
+        step_bytes = (12 * E * E * L + V * E) * 4 + L * rows * ctx * 2 * E * 4
+        add("decode_step", measured.get("decode_step"), steps, "hbm", step_bytes)
+    elif steps > 0:
         kv_bytes = rows * ctx * 2 * E * 4 + rows * 2 * E * 4
         add("decode_attention", measured.get("decode_attention"), L * steps, "hbm", kv_bytes)
         for name, N, K in (("decode_qkv", 3 * E, E), ("decode_fc", 4 * E, E), ("decode_mlp_proj", E, 4 * E)):
@@ -354,8 +363,12 @@ def run_ours(args, rank, local_rank, world):
     # per-kernel live timings at this rank's shapes
     measured = {}
     ctx = T + n_new // 2
-    names = (["decode_attention", "decode_qkv", "decode_fc", "decode_mlp_proj", "decode_head"]
-             if n_new > 1 else ["prefill_fc", "prefill_attention"])
+    if n_new > 1 and size <= STEP_ROWS:
+        names = ["decode_step"]
+    elif n_new > 1:
+        names = ["decode_attention", "decode_qkv", "decode_fc", "decode_mlp_proj", "decode_head"]
+    else:
+        names = ["prefill_fc", "prefill_attention"]
     for name in names:
         measured[name] = m.time_kernel(name, size, ctx if name.startswith("decode") else T, iters=20)
     peaks = {}

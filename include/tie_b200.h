@@ -98,7 +98,9 @@ model_status model_generate_greedy_device(model *m, const int32_t *d_prompts, si
  *   TIE_KERNEL_DECODE_MLP_PROJ   the MLP down-projection (+ residual)
  *   TIE_KERNEL_DECODE_HEAD       the tied head with its fused argmax
  *   TIE_KERNEL_PREFILL_ATTENTION causal attention over `context` tokens x `rows`
- *   TIE_KERNEL_PREFILL_FC        the MLP up-projection over rows * context tokens */
+ *   TIE_KERNEL_PREFILL_FC        the MLP up-projection over rows * context tokens
+ *   TIE_KERNEL_DECODE_STEP       one whole decode step of `rows` (<= 4) sequences
+ *                                at context `context` as the persistent kernel */
 enum {
     TIE_KERNEL_DECODE_ATTENTION = 0,
     TIE_KERNEL_DECODE_QKV = 1,
@@ -106,10 +108,40 @@ enum {
     TIE_KERNEL_DECODE_MLP_PROJ = 3,
     TIE_KERNEL_DECODE_HEAD = 4,
     TIE_KERNEL_PREFILL_ATTENTION = 5,
-    TIE_KERNEL_PREFILL_FC = 6
+    TIE_KERNEL_PREFILL_FC = 6,
+    TIE_KERNEL_DECODE_STEP = 7
 };
 model_status model_time_kernel(model *m, int kernel, size_t rows, size_t context, int iters,
                                float *avg_ms);
+
+/* The last CUDA failure behind a MODEL_ERR_DEVICE on the calling thread: the
+ * error's name and text and the failing call, or "" if none yet. With the
+ * environment variable TIE_DEBUG set, each such failure is also printed to
+ * stderr. */
+const char *tie_last_device_error(void);
+
+/* ---- how small decode steps run ------------------------------------------
+ * A decode step of at most 4 sequences (without attention statistics) runs as
+ * ONE persistent kernel per step: TIE_STEP_PERSISTENT, the default. With
+ * TIE_STEP_CHAINED it runs as the chain of per-layer kernels that batches of
+ * 5..16 sequences use. Both form every sum in the same order, so they return
+ * identical logits and tokens; the switch exists to compare and time them.
+ * MODEL_ERR_ARG for any other value. */
+enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1 };
+model_status model_set_step_kernel(model *m, int kind);
+
+/* Trace of one persistent decode step of `rows` (<= 4) sequences at context
+ * `context` on the batch pool (model_batch_reserve must cover them; contents
+ * are overwritten as for model_time_kernel): per CTA, *per_cta global-timer
+ * stamps in nanoseconds, *n_cta CTAs, written to out (host, cap >= per_cta *
+ * n_cta, else MODEL_ERR_CAPACITY after filling the two counts). Stamp order per
+ * CTA: [0] start; [1 + 3 * (5 * layer + stage) + k] for stage 0..4 (LN1+qkv,
+ * attention, proj, LN2+fc, mlp) with k = 0 inputs ready, 1 rows staged, 2 done,
+ * the head as stage 5 * n_layer; then the CTA's end; then, per weight matrix in
+ * stream order (qkv, proj, fc, mlp per layer, then wte), when its last copy was
+ * issued. */
+model_status model_step_trace(model *m, size_t rows, size_t context, uint64_t *out, size_t cap,
+                              size_t *per_cta, size_t *n_cta);
 
 /* ---- the greedy head without allocation --------------------------------
  * No counterpart in the reference (its head is a CPU matmul over host memory).

@@ -65,6 +65,60 @@ __device__ __forceinline__ float apply_epi(float acc, const float* __restrict__ 
     }
 }
 
+// ------------------------------------------------------------- LayerNorm --
+// The engine's one LayerNorm arithmetic (model.c:593-610 in double, summed in a
+// fixed order of its own): mean and biased variance in double, inv =
+// (float)(1 / sqrt(var + eps)), y = fl(fl(fl((x - mean) * inv) * g) + b).
+// Both sums run in the canonical order below, whichever kernel computes them,
+// so every path normalises a row to the same bits:
+//   256 virtual lanes v = 32 w + l (w = 0..7, l = 0..31); lane v adds its terms
+//   i = v, v + 256, v + 512, ... in increasing i; each group w of 32 lanes is
+//   reduced by an xor butterfly (offsets 16, 8, 4, 2, 1); the group sums are
+//   added in group order, G0 + G1 + ... + G7.
+constexpr int kLnGroups = 8;
+
+__device__ __forceinline__ double ln_warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Group w's sum (every lane of the calling warp gets it): lane l adds the
+// terms of virtual lane 32 w + l, then the butterfly.
+template <typename Term>
+__device__ __forceinline__ double ln_group_sum(const Term& term, int K, int w, int lane) {
+    double s = 0.0;
+    for (int i = 32 * w + lane; i < K; i += 32 * kLnGroups) s = __dadd_rn(s, term(i));
+    return ln_warp_sum_d(s);
+}
+
+// The whole canonical sum by one warp.
+template <typename Term>
+__device__ __forceinline__ double ln_sum_warp(const Term& term, int K, int lane) {
+    double S = ln_group_sum(term, K, 0, lane);
+#pragma unroll 1
+    for (int w = 1; w < kLnGroups; ++w) S = __dadd_rn(S, ln_group_sum(term, K, w, lane));
+    return S;
+}
+
+// mean and inv of row xr (K floats, any memory) by one warp
+__device__ __forceinline__ void ln_stats_warp(const float* xr, int K, float eps, int lane, double& mean,
+                                              float& inv) {
+    const double S = ln_sum_warp([&](int i) { return (double)xr[i]; }, K, lane);
+    mean = S / (double)K;
+    const double m = mean;
+    const double V = ln_sum_warp([&](int i) {
+        const double d = __dadd_rn((double)xr[i], -m);
+        return __dmul_rn(d, d);
+    }, K, lane);
+    inv = (float)(1.0 / sqrt(__dadd_rn(V / (double)K, (double)eps)));
+}
+
+__device__ __forceinline__ float ln_apply(float x, double mean, float inv, float g, float b) {
+    const float nrm = (float)__dmul_rn(__dadd_rn((double)x, -mean), (double)inv);
+    return __fadd_rn(__fmul_rn(nrm, g), b);
+}
+
 // ------------------------------------------------------------ paged KV view --
 // One layer's keys and values: rows of n_embd floats grouped into pages of
 // kPageRows positions. Position p of sequence s lives at physical row
@@ -156,7 +210,7 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
 cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
                             int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st);
-int dec_head_blocks(int V);
+int dec_head_blocks(int V, int K);
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
                             int* part_idx, cudaStream_t st);
@@ -171,5 +225,66 @@ cudaError_t launch_gemm_naive(int M, int N, int K, const float* A, int lda, cons
                               int ldb, float* C, int ldc, bool bt, cudaStream_t st);
 // out[c][r] = in[r][c] for an R x Cc matrix (load-time weight transpose)
 cudaError_t launch_transpose(const float* in, float* out, int R, int Cc, cudaStream_t st);
+
+// ------------------------------------------------- the persistent decode step --
+// One layer's weights as the persistent step kernel reads them (k_step.cu).
+struct StepLayer {
+    const float *ln1_g, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
+    const float *ln2_g, *ln2_b, *fc_w, *fc_b, *mlp_w, *mlp_b;
+};
+
+struct StepParams {
+    const StepLayer* layers;     // [n_layer], device memory
+    int n_layer, E, H, V, M;     // M: sequences of the step (1..4)
+    float eps, scale;            // LayerNorm epsilon, attention 1/sqrt(head dim)
+    const float *wte, *wpe, *lnf_g, *lnf_b;
+    // the paged cache: layer l's rows start at k + l * layer_stride
+    float *k, *v;
+    size_t layer_stride;
+    const int* page_table;
+    int pages_per_seq;
+    int max_splits;              // attention partial slots per (sequence, head)
+    int32_t *tokens, *lens;      // this step's input token and position per sequence
+    float *x, *qkv, *attn, *ff;  // activations, rows of E, 3E, E, 4E
+    float* logits;               // [M][ldl] or NULL
+    int ldl;
+    float* part;                 // attention partials
+    int* head_cnt;               // [M * H] arrival counters, zero between steps
+    unsigned* sync;              // [step_sync_words] stage counters, zero between steps
+    float* am_val;               // [grid][M] per-CTA argmax partials
+    int* am_idx;
+    int32_t* next;               // [M] argmax
+    int advance;                 // tokens = next, lens += 1, out[m][*step] = next, *step += 1
+    int32_t* out;
+    int ld_out;
+    int32_t* step;
+    int* err;                    // set when a bounded wait expires
+    int slots;                   // ring slots (from step_supported)
+    int head_prefetch;           // bytes of its head rows each CTA prefetches into L2 during the layers
+    unsigned long long* trace;   // [grid][step_trace_events] global-timer stamps, or NULL
+};
+
+// Whether the persistent step runs M sequences of a model of width E with H
+// heads and n_layer layers on the current device; fills the ring slots and the
+// grid (one CTA per SM). Each launch also needs a cache of at most
+// step_max_pages() pages per sequence.
+bool step_supported(int M, int E, int H, int n_layer, int* slots, int* grid);
+int step_max_pages();
+// The whole decode step in one cooperative launch.
+cudaError_t launch_step(const StepParams& p, int grid, cudaStream_t st);
+// Counters the step kernel needs zeroed: 5 per layer + 1.
+inline size_t step_sync_words(int n_layer) { return 5 * (size_t)n_layer + 1; }
+
+// Trace of one step, per CTA (global-timer nanoseconds):
+//   [0]                           the consumers start
+//   [1 + 3 * (5 * l + s) + k]     stage s (0..4 = A..E) of layer l; the head is
+//                                 stage 5 * n_layer; k = 0 inputs ready (the
+//                                 wait is over), 1 activation rows staged,
+//                                 2 stage done
+//   [step_trace_end(L)]           this CTA done
+//   [step_trace_end(L) + 1 + i]   the producer has issued all of matrix i
+//                                 (4 per layer: qkv, proj, fc, mlp; then wte)
+__host__ __device__ inline int step_trace_end(int n_layer) { return 1 + 3 * (5 * n_layer + 1); }
+__host__ __device__ inline int step_trace_events(int n_layer) { return step_trace_end(n_layer) + 1 + 4 * n_layer + 1; }
 
 }  // namespace tie

@@ -34,17 +34,11 @@ __device__ __forceinline__ float4 ld_stream(const float* p) {
     return v;
 }
 
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 // LayerNorm of rows [0, M) of x (row stride ldx) into xs (row stride K), the
 // arithmetic of layernorm_kernel (k_misc.cu). Each row is first copied into
-// xs with all of the block's 16-byte loads in flight at once; the statistics
-// (one warp per row, double precision) and the normalisation then run out of
-// shared memory, in place.
+// xs with all of the block's 16-byte loads in flight; the statistics (one warp
+// per row, the canonical order of ln_stats_warp) and the normalisation then
+// run out of shared memory, in place.
 __device__ void ln_rows_to_smem(const float* __restrict__ x, int ldx, const float* __restrict__ g,
                                 const float* __restrict__ b, float eps, int M, int K, float* xs) {
     const int K4 = K >> 2;
@@ -57,22 +51,10 @@ __device__ void ln_rows_to_smem(const float* __restrict__ x, int ldx, const floa
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int m = warp; m < M; m += kWarps) {
         float* xr = xs + (size_t)m * K;
-        double s = 0.0;
-        for (int i = lane; i < K; i += 32) s = __dadd_rn(s, (double)xr[i]);
-        s = warp_sum_d(s);
-        const double mean = s / (double)K;
-        double v = 0.0;
-        for (int i = lane; i < K; i += 32) {
-            const double d = __dadd_rn((double)xr[i], -mean);
-            v = __dadd_rn(v, __dmul_rn(d, d));
-        }
-        v = warp_sum_d(v);
-        v = v / (double)K;
-        const float inv = (float)(1.0 / sqrt(__dadd_rn(v, (double)eps)));
-        for (int i = lane; i < K; i += 32) {
-            const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
-            xr[i] = __fadd_rn(__fmul_rn(nrm, g[i]), b[i]);
-        }
+        double mean;
+        float inv;
+        ln_stats_warp(xr, K, eps, lane, mean, inv);
+        for (int i = lane; i < K; i += 32) xr[i] = ln_apply(xr[i], mean, inv, g[i], b[i]);
     }
 }
 
@@ -274,7 +256,12 @@ cudaError_t dec_dispatch(const DecArgs& a, cudaStream_t st) {
 
 }  // namespace
 
-int dec_head_blocks(int V) { return (V + kWarps * 4 - 1) / (kWarps * 4); }  // RPW 4, WS 1
+// Rows per head block: 4 rows in each of 4 warps while a row is at most 256
+// chunks (RPW 4, WS 1), else one row cut into 4 slices (RPW 1, WS 4).
+int dec_head_blocks(int V, int K) {
+    const int rows = (K >> 2) <= 256 ? kWarps * 4 : 1;
+    return (V + rows - 1) / rows;
+}
 
 // y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL.
 cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
@@ -309,8 +296,12 @@ cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const fl
     DecArgs a{};
     a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W;
     a.y = logits; a.ldy = ldl; a.M = M; a.N = V; a.K = K; a.part_val = part_val; a.part_idx = part_idx;
-    if ((K >> 2) > 256) return cudaErrorInvalidValue;  // the head's K is n_embd
-    return ln_g ? dec_launch<DEC_HEAD, true, 4, 1, 8>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8>(a, st);
+    const int K4 = K >> 2;
+    if (K4 <= 256)
+        return ln_g ? dec_launch<DEC_HEAD, true, 4, 1, 8>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8>(a, st);
+    if (K4 <= 1024)
+        return ln_g ? dec_launch<DEC_HEAD, true, 1, 4, 8>(a, st) : dec_launch<DEC_HEAD, false, 1, 4, 8>(a, st);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace tie

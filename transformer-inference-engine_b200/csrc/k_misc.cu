@@ -10,12 +10,6 @@ namespace tie {
 
 namespace {
 
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 // ------------------------------------------------------------- embedding --
 // model.c:671-676 / 805-809: x = wte[id] + wpe[pos], one float add per element.
 // An id outside [0, V) (only possible through the device-buffer entry point,
@@ -67,11 +61,10 @@ __global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
 }
 
 // ------------------------------------------------------------- LayerNorm --
-// model.c:593-610: mean and biased variance in double, inv = (float)(1/sqrt(var
-// + eps)), normalized = (float)((x - mean) * inv), then a float multiply by the
-// gain and a float add of the shift, each rounded separately. One warp per row;
-// the row is first staged in shared memory with all its 16-byte loads in
-// flight, so the statistics do not wait on one load at a time.
+// model.c:593-610 with the engine's canonical summation order (ln_stats_warp,
+// common.cuh). One warp per row; the row is first staged in shared memory
+// with all its 16-byte loads in flight, so the statistics do not wait on one
+// load at a time.
 constexpr int kLnWarps = 4;
 constexpr int kLnMaxK = 2048;
 
@@ -89,22 +82,12 @@ layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * E);
     for (int c = lane; c < E4; c += 32) reinterpret_cast<float4*>(xr)[c] = src[c];
     __syncwarp();
-    double s = 0.0;
-    for (int i = lane; i < E; i += 32) s = __dadd_rn(s, (double)xr[i]);
-    s = warp_sum_d(s);
-    const double mean = s / (double)E;
-    double v = 0.0;
-    for (int i = lane; i < E; i += 32) {
-        const double d = __dadd_rn((double)xr[i], -mean);
-        v = __dadd_rn(v, __dmul_rn(d, d));
-    }
-    v = warp_sum_d(v);
-    v = v / (double)E;
-    const float inv = (float)(1.0 / sqrt(__dadd_rn(v, (double)eps)));
+    double mean;
+    float inv;
+    ln_stats_warp(xr, E, eps, lane, mean, inv);
     const size_t off = (size_t)row * E;
     for (int i = lane; i < E; i += 32) {
-        const float nrm = (float)__dmul_rn(__dadd_rn((double)xr[i], -mean), (double)inv);
-        const float val = __fadd_rn(__fmul_rn(nrm, g[i]), bvec[i]);
+        const float val = ln_apply(xr[i], mean, inv, g[i], bvec[i]);
         if (y) y[off + i] = val;
         if (y_hi) {
             const float h = tf32_hi(val);

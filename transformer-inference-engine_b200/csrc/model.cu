@@ -18,6 +18,7 @@
 #include "internal.h"
 #include "tc_gemm.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -226,22 +227,41 @@ struct model {
 
     kv_cache* pool = nullptr;
     std::map<GraphKey, GraphEntry> graphs;
+
+    // the persistent decode step (k_step.cu)
+    int step_kind = TIE_STEP_PERSISTENT;
+    StepLayer* d_step_layers = nullptr;
+    unsigned* d_sync = nullptr;      // the step kernel's stage counters
+    int step_state[5] = {0, 0, 0, 0, 0};  // per batch size: 0 unknown, 1 runs, -1 does not
+    int step_slots[5] = {0, 0, 0, 0, 0};
+    int step_grid = 0;
     uint64_t launches = 0;
 };
 
 namespace {
 
+// The last CUDA error a model call hit on this thread (tie_last_device_error),
+// and, with TIE_DEBUG set in the environment, one line per failure on stderr.
+thread_local char g_dev_err[256] = "";
+
+void note_cuda(cudaError_t e, const char* what, int line) {
+    std::snprintf(g_dev_err, sizeof g_dev_err, "%s (%s) at model.cu:%d: %s", cudaGetErrorName(e),
+                  cudaGetErrorString(e), line, what);
+    static const bool verbose = std::getenv("TIE_DEBUG") != nullptr;
+    if (verbose) std::fprintf(stderr, "tie_b200: %s\n", g_dev_err);
+}
+
 #define CU(expr)                                                   \
     do {                                                           \
         cudaError_t e_ = (expr);                                   \
-        if (e_ != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; } \
+        if (e_ != cudaSuccess) { note_cuda(e_, #expr, __LINE__); cudaGetLastError(); return MODEL_ERR_DEVICE; } \
     } while (0)
 
 #define LAUNCH(expr)                                               \
     do {                                                           \
         cudaError_t e_ = (expr);                                   \
         ++m->launches;                                             \
-        if (e_ != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; } \
+        if (e_ != cudaSuccess) { note_cuda(e_, #expr, __LINE__); cudaGetLastError(); return MODEL_ERR_DEVICE; } \
     } while (0)
 
 void drop_graphs(model* m) {
@@ -330,7 +350,10 @@ model_status ensure_slots(model* m, size_t B, int capacity) {
         if ((rc = grow(&m->d_attn_cnt, &m->cnt_cap, cnt)) != MODEL_OK) return rc;
         CU(cudaMemset(m->d_attn_cnt, 0, cnt * sizeof(int)));
     }
-    const size_t parts = (size_t)gemv_argmax_blocks(m->cfg.vocab_size) * B;
+    int sms = 0;
+    CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device));
+    const size_t parts = (size_t)std::max({gemv_argmax_blocks(m->cfg.vocab_size),
+                                           dec_head_blocks(m->cfg.vocab_size, m->cfg.n_embd), sms}) * B;
     if (parts > m->am_parts) {
         drop_graphs(m);
         size_t c1 = m->am_parts, c2 = m->am_parts;
@@ -490,7 +513,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
         }
         LAUNCH(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
                                m->d_am_idx, st));
-        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V), B, m->d_next, st));
+        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E), B, m->d_next, st));
         if (advance)
             LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
         return MODEL_OK;
@@ -527,8 +550,74 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
 }
 
 // Runs one decode step, from a graph when statistics are off.
+// Whether a step of B sequences takes the persistent kernel; allocates its
+// layer table and counters on first use.
+bool use_step(model* m, int B, const kv_cache* cache) {
+    if (m->step_kind != TIE_STEP_PERSISTENT || m->stats_on || B < 1 || B > 4) return false;
+    if (!cache || cache->pages_per_seq > step_max_pages()) return false;
+    int& state = m->step_state[B];
+    if (state == 0) {
+        int grid = 0;
+        state = step_supported(B, m->cfg.n_embd, m->cfg.n_head, m->cfg.n_layer, &m->step_slots[B], &grid) ? 1 : -1;
+        if (state == 1) m->step_grid = grid;
+    }
+    if (state != 1) return false;
+    if (!m->d_step_layers) {
+        const int L = m->cfg.n_layer;
+        std::vector<StepLayer> table((size_t)L);
+        for (int l = 0; l < L; ++l) {
+            const Layer& w = m->layers[l];
+            table[l] = StepLayer{w.ln1_w, w.ln1_b, w.qkv_w, w.qkv_b, w.proj_w, w.proj_b,
+                                 w.ln2_w, w.ln2_b, w.fc_w, w.fc_b, w.mlp_w, w.mlp_b};
+        }
+        StepLayer* d = nullptr;
+        unsigned* c = nullptr;
+        const size_t words = step_sync_words(L);
+        if (cudaMalloc(&d, table.size() * sizeof(StepLayer)) != cudaSuccess ||
+            cudaMalloc(&c, words * sizeof(unsigned)) != cudaSuccess ||
+            cudaMemcpy(d, table.data(), table.size() * sizeof(StepLayer), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(c, 0, words * sizeof(unsigned)) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(d);
+            cudaFree(c);
+            state = -1;
+            return false;
+        }
+        m->d_sync = c;
+        m->d_step_layers = d;
+    }
+    return true;
+}
+
+// The whole decode step of B <= 4 sequences as one persistent kernel.
+model_status run_step(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out,
+                      unsigned long long* trace = nullptr) {
+    StepParams p{};
+    p.layers = m->d_step_layers;
+    p.n_layer = m->cfg.n_layer; p.E = m->cfg.n_embd; p.H = m->cfg.n_head; p.V = m->cfg.vocab_size; p.M = B;
+    p.eps = m->cfg.layer_norm_epsilon;
+    p.scale = (float)(1.0 / std::sqrt((double)(m->cfg.n_embd / m->cfg.n_head)));
+    p.wte = m->wte; p.wpe = m->wpe; p.lnf_g = m->lnf_w; p.lnf_b = m->lnf_b;
+    p.k = cache->k; p.v = cache->v; p.layer_stride = cache->rows * (size_t)m->cfg.n_embd;
+    p.page_table = cache->d_page_table; p.pages_per_seq = cache->pages_per_seq;
+    p.max_splits = attn_decode_max_splits(cache->capacity);
+    p.tokens = m->d_tokens; p.lens = m->d_lens;
+    p.x = m->x; p.qkv = m->qkv; p.attn = m->attn; p.ff = m->ff;
+    p.logits = m->logits; p.ldl = m->cfg.vocab_size;
+    p.part = m->d_part; p.head_cnt = m->d_attn_cnt; p.sync = m->d_sync;
+    p.am_val = m->d_am_val; p.am_idx = m->d_am_idx; p.next = m->d_next;
+    p.advance = advance ? 1 : 0; p.out = out; p.ld_out = ld_out; p.step = m->d_step;
+    p.err = m->d_err; p.slots = m->step_slots[B]; p.trace = trace;
+    // about 60% of the tied head (92 MB for GPT-2) fits in L2 beside the KV cache
+    p.head_prefetch = (int)std::min<size_t>((size_t)1 << 30,
+                                            (size_t)m->cfg.vocab_size * m->cfg.n_embd * 4 * 6 / 10 / m->step_grid);
+    LAUNCH(launch_step(p, m->step_grid, m->st));
+    return MODEL_OK;
+}
+
 model_status decode_step(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
     if (m->stats_on) return run_decode(m, B, cache, advance, out, ld_out);
+    if (use_step(m, B, cache)) return run_step(m, B, cache, advance, out, ld_out);
     const GraphKey key{B, cache, advance, out, ld_out};
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
@@ -576,7 +665,13 @@ model_status finish(model* m) {
         int err = 0;
         CU(cudaMemcpy(&err, m->d_err, sizeof err, cudaMemcpyDeviceToHost));
         if (err) {
+            std::snprintf(g_dev_err, sizeof g_dev_err, "a kernel's bounded wait expired (device error flag %d)", err);
+            if (std::getenv("TIE_DEBUG")) std::fprintf(stderr, "tie_b200: %s\n", g_dev_err);
             cudaMemset(m->d_err, 0, sizeof(int));
+            // a step that gave up leaves its counters wherever it stopped
+            if (m->d_sync) cudaMemset(m->d_sync, 0, step_sync_words(m->cfg.n_layer) * sizeof(unsigned));
+            if (m->d_attn_cnt) cudaMemset(m->d_attn_cnt, 0, m->cnt_cap * sizeof(int));
+            if (m->d_attn_cnt) cudaMemset(m->d_attn_cnt, 0, m->cnt_cap * sizeof(int));
             return MODEL_ERR_DEVICE;
         }
     }
@@ -853,6 +948,8 @@ fail:
 // ================================================================== the ABI ==
 extern "C" {
 
+const char* tie_last_device_error(void) { return g_dev_err; }
+
 const char* model_strerror(model_status s) {
     switch (s) {
         case MODEL_OK: return "ok";
@@ -897,6 +994,7 @@ void model_free(model* m) {
     cudaFree(m->d_tokens); cudaFree(m->d_lens); cudaFree(m->d_next); cudaFree(m->d_step);
     cudaFree(m->d_out); cudaFree(m->d_part); cudaFree(m->d_attn_cnt); cudaFree(m->d_am_val); cudaFree(m->d_am_idx);
     cudaFree(m->d_stats);
+    cudaFree(m->d_step_layers); cudaFree(m->d_sync);
     if (m->h_small) cudaFreeHost(m->h_small);
     kv_cache_destroy(m->kv);
     kv_cache_destroy(m->pool);
@@ -1236,6 +1334,40 @@ model_status model_generate_greedy_device(model* m, const int32_t* d_prompts, si
     return generate_impl(m, d_prompts, n_seq, n_prompt, n_new, d_out_ids, false);
 }
 
+model_status model_step_trace(model* m, size_t rows, size_t context, uint64_t* out, size_t cap,
+                              size_t* per_cta, size_t* n_cta) {
+    if (!m || !per_cta || !n_cta || rows == 0 || rows > 4 || context == 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)rows > m->pool->n_seq || (int)context > m->pool->capacity) return MODEL_ERR_CAPACITY;
+    model_status rc = ensure_slots(m, rows, m->pool->capacity);
+    if (rc != MODEL_OK) return rc;
+    if (!use_step(m, (int)rows, m->pool)) return MODEL_ERR_ARG;
+    const size_t ev = (size_t)step_trace_events(m->cfg.n_layer), G = (size_t)m->step_grid;
+    *per_cta = ev;
+    *n_cta = G;
+    if (!out || cap < ev * G) return MODEL_ERR_CAPACITY;
+    std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
+    if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    unsigned long long* d = nullptr;
+    CU(cudaMalloc(&d, ev * G * sizeof(unsigned long long)));
+    CU(cudaMemsetAsync(d, 0, ev * G * sizeof(unsigned long long), m->st));
+    rc = run_step(m, (int)rows, m->pool, false, nullptr, 0);  // warm
+    if (rc == MODEL_OK) rc = run_step(m, (int)rows, m->pool, false, nullptr, 0, d);
+    if (rc == MODEL_OK && cudaMemcpyAsync(out, d, ev * G * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                                          m->st) != cudaSuccess)
+        rc = MODEL_ERR_DEVICE;
+    if (rc == MODEL_OK) rc = finish(m);
+    cudaStreamSynchronize(m->st);
+    cudaFree(d);
+    return rc;
+}
+
+model_status model_set_step_kernel(model* m, int kind) {
+    if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED)) return MODEL_ERR_ARG;
+    if (kind != m->step_kind) drop_graphs(m);
+    m->step_kind = kind;
+    return MODEL_OK;
+}
+
 model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context, int iters,
                                float* avg_ms) {
     if (!m || !avg_ms || rows == 0 || context == 0 || iters <= 0) return MODEL_ERR_ARG;
@@ -1298,7 +1430,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                 if (small) {
                     CU(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, m->cfg.layer_norm_epsilon, m->wte, m->logits, V,
                                        B, V, E, m->d_am_val, m->d_am_idx, st));
-                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V), B, m->d_next, st));
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E), B, m->d_next, st));
                     return MODEL_OK;
                 } else {
                     model_status r = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr,
@@ -1313,6 +1445,10 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
             case TIE_KERNEL_PREFILL_FC:
                 return matmul(m, false, (int)R, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b,
                               EPI_BIAS_GELU, nullptr, m->ff_hi, m->ff_lo, 4 * E);
+            case TIE_KERNEL_DECODE_STEP:
+                // the step without advancing: every launch sees the same lengths
+                if (!use_step(m, B, m->pool)) return MODEL_ERR_ARG;
+                return run_step(m, B, m->pool, false, nullptr, 0);
         }
         return MODEL_ERR_ARG;
     };

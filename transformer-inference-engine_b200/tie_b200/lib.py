@@ -19,6 +19,7 @@ KV_STATUS = ["KV_OK", "KV_ERR_ARG", "KV_ERR_CAPACITY", "KV_ERR_NOMEM"]
 for _i, _n in enumerate(MODEL_STATUS + KV_STATUS):
     globals()[_n] = _i if _n in MODEL_STATUS else KV_STATUS.index(_n)
 MODEL_PATH_NOCACHE, MODEL_PATH_CACHE = 0, 1
+TIE_STEP_PERSISTENT, TIE_STEP_CHAINED = 0, 1
 MODEL_CPROJ_AS_STORED, MODEL_CPROJ_TRANSPOSED = 0, 1
 
 _fp = C.POINTER(C.c_float)
@@ -116,6 +117,10 @@ def library():
         "model_generate_greedy": (C.c_int, [_vp, _ip, C.c_size_t, C.c_size_t, C.c_size_t, _ip]),
         "model_generate_greedy_device": (C.c_int, [_vp, _vp, C.c_size_t, C.c_size_t, C.c_size_t, _vp]),
         "model_time_kernel": (C.c_int, [_vp, C.c_int, C.c_size_t, C.c_size_t, C.c_int, _fp]),
+        "model_set_step_kernel": (C.c_int, [_vp, C.c_int]),
+        "model_step_trace": (C.c_int, [_vp, C.c_size_t, C.c_size_t, _vp, C.c_size_t,
+                                       C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+        "tie_last_device_error": (C.c_char_p, []),
         "tie_head_argmax_noalloc": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                               _vp, C.c_int, _vp, _vp]),
         "kv_cache_footprint_for": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
@@ -161,7 +166,11 @@ class ModelError(RuntimeError):
         self.status = status
         name = MODEL_STATUS[status] if 0 <= status < len(MODEL_STATUS) else str(status)
         msg = library().model_strerror(status).decode()
-        super().__init__(f"{where}: {name} ({msg})")
+        detail = ""
+        if name == "MODEL_ERR_DEVICE":
+            detail = (library().tie_last_device_error() or b"").decode()
+            detail = f" [{detail}]" if detail else ""
+        super().__init__(f"{where}: {name} ({msg}){detail}")
 
 
 def _chk(rc, where):
@@ -271,6 +280,19 @@ class Model:
 
     def set_decode_path(self, p):
         library().model_set_decode_path(self.h, p)
+
+    def set_step_kernel(self, kind):
+        """TIE_STEP_PERSISTENT (default) or TIE_STEP_CHAINED for decode steps of <= 4 sequences."""
+        _chk(library().model_set_step_kernel(self.h, kind), "model_set_step_kernel")
+
+    def step_trace(self, rows: int, context: int) -> np.ndarray:
+        """Global-timer stamps (ns) of one persistent decode step: [n_cta, per_cta]."""
+        per, n = C.c_size_t(), C.c_size_t()
+        library().model_step_trace(self.h, rows, context, None, 0, C.byref(per), C.byref(n))
+        out = np.zeros((n.value, per.value), dtype=np.uint64)
+        _chk(library().model_step_trace(self.h, rows, context, out.ctypes.data_as(_vp), out.size,
+                                        C.byref(per), C.byref(n)), "model_step_trace")
+        return out
 
     def decode_path(self):
         return library().model_decode_path_of(self.h)
@@ -383,7 +405,7 @@ class Model:
         return rc, out
 
     KERNELS = {"decode_attention": 0, "decode_qkv": 1, "decode_fc": 2, "decode_mlp_proj": 3,
-               "decode_head": 4, "prefill_attention": 5, "prefill_fc": 6}
+               "decode_head": 4, "prefill_attention": 5, "prefill_fc": 6, "decode_step": 7}
 
     def time_kernel(self, name: str, rows: int, context: int, iters: int = 20) -> float:
         """Average milliseconds per launch of one kernel, alone (model_time_kernel)."""
