@@ -44,8 +44,13 @@ WORKLOADS = {
     "prefill": dict(shape="small", n_seq=8, n_prompt=1024, n_new=1, prompt_seed=102),
     # GPT-2 medium fp32, batch 8, prompt 512, greedy 256
     "medium": dict(shape="medium", n_seq=8, n_prompt=512, n_new=256, prompt_seed=103),
+    # GPT-2 medium with bf16 weights (fp32 accumulate)
+    "medium_bf16": dict(shape="medium", n_seq=8, n_prompt=512, n_new=256, prompt_seed=103, fmt="bf16"),
     # GPT-2 XL fp32, batch 1, prompt 896, greedy 128
     "xl": dict(shape="xl", n_seq=1, n_prompt=896, n_new=128, prompt_seed=104),
+    # GPT-2 XL with bf16 / int8 per-output-channel weights (fp32 accumulate)
+    "xl_bf16": dict(shape="xl", n_seq=1, n_prompt=896, n_new=128, prompt_seed=104, fmt="bf16"),
+    "xl_int8": dict(shape="xl", n_seq=1, n_prompt=896, n_new=128, prompt_seed=104, fmt="int8"),
     # a small case of the throughput shapes, for profiler captures
     "probe": dict(shape="small", n_seq=64, n_prompt=64, n_new=16, prompt_seed=105),
 }
@@ -203,8 +208,12 @@ def run_reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------- our arm --
-# decode steps of at most this many sequences run as one persistent kernel
+# fp32 decode steps of at most this many sequences run as one persistent kernel
 STEP_ROWS = 4
+
+
+def weight_bytes_per_elem(wl):
+    return {"f32": 4, "bf16": 2, "int8": 1}[wl.get("fmt", "f32")]
 
 
 def roofline_of(m, wl, rows, measured, peaks):
@@ -229,7 +238,7 @@ def roofline_of(m, wl, rows, measured, peaks):
         k[name]["share_ms"] = ms * per_step
         k[name]["work_per_launch"] = work
 
-    if steps > 0 and rows <= STEP_ROWS:
+    if steps > 0 and rows <= STEP_ROWS and wl.get("fmt", "f32") == "f32":
         # the persistent step kernel: every weight matrix once, the KV cache of
         # every layer once, per step
         step_bytes = (12 * E * E * L + V * E) * 4 + L * rows * ctx * 2 * E * 4
@@ -240,11 +249,12 @@ def roofline_of(m, wl, rows, measured, peaks):
         for name, N, K in (("decode_qkv", 3 * E, E), ("decode_fc", 4 * E, E), ("decode_mlp_proj", E, 4 * E)):
             ms = measured.get(name)
             if rows <= 16:
-                add(name, ms, L * steps, "hbm", N * K * 4 + rows * (N + K) * 4)
+                add(name, ms, L * steps, "hbm", N * K * weight_bytes_per_elem(wl) + rows * (N + K) * 4)
             else:
                 add(name, ms, L * steps, "tensor", 2.0 * rows * N * K)
         if rows <= 16:
-            add("decode_head", measured.get("decode_head"), steps, "hbm", V * E * 4 + rows * V * 4)
+            add("decode_head", measured.get("decode_head"), steps, "hbm",
+                V * E * weight_bytes_per_elem(wl) + rows * V * 4)
         else:
             add("decode_head", measured.get("decode_head"), steps, "tensor", 2.0 * rows * V * E)
     else:
@@ -296,6 +306,9 @@ def run_ours(args, rank, local_rank, world):
     T, n_new = wl["n_prompt"], wl["n_new"]
 
     m = tie_b200.Model(w, inv, cfg, device=local_rank)
+    fmt = wl.get("fmt", "f32")
+    if fmt != "f32":
+        m.set_weight_format({"bf16": tie_b200.TIE_WEIGHTS_BF16, "int8": tie_b200.TIE_WEIGHTS_INT8}[fmt])
     m.batch_reserve(size, T + n_new - 1)
     stream = torch.cuda.ExternalStream(m.stream)
     d_prompts = torch.from_numpy(prompts).to("cuda")
@@ -363,7 +376,7 @@ def run_ours(args, rank, local_rank, world):
     # per-kernel live timings at this rank's shapes
     measured = {}
     ctx = T + n_new // 2
-    if n_new > 1 and size <= STEP_ROWS:
+    if n_new > 1 and size <= STEP_ROWS and fmt == "f32":
         names = ["decode_step"]
     elif n_new > 1:
         names = ["decode_attention", "decode_qkv", "decode_fc", "decode_mlp_proj", "decode_head"]
@@ -382,7 +395,8 @@ def run_ours(args, rank, local_rank, world):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "f32",
+                "vs_baseline": None,
+                "dtype": "f32" if fmt == "f32" else f"{fmt} weights, f32 accumulate",
                 "data": "synthetic (seeded random-init weights, seeded uniform token ids)",
                 "config": {"workload": args.workload, "model": f"gpt2-{wl['shape']}", "n_seq": wl["n_seq"],
                            "n_prompt": T, "n_new": n_new, "seq_per_gpu": size,

@@ -114,6 +114,25 @@ enum {
 model_status model_time_kernel(model *m, int kernel, size_t rows, size_t context, int iters,
                                float *avg_ms);
 
+/* ---- weight formats --------------------------------------------------------
+ * The reference computes in fp32 only. These formats trade weight precision
+ * for HBM traffic in the memory-bound decode:
+ *   TIE_WEIGHTS_F32   the loaded weights (the default).
+ *   TIE_WEIGHTS_BF16  each matrix element rounded to nearest-even bf16.
+ *   TIE_WEIGHTS_INT8  per output channel (a row of each [out, in] matrix):
+ *                     scale = absmax(row) / 127 in fp32, q = rint(w / scale)
+ *                     (ties to even) clamped to +-127; the weight is q * scale.
+ * The formats apply to the five matrix kinds -- qkv, attention proj, fc, mlp
+ * proj, and the tied wte (head and embedding lookup alike); LayerNorm, biases
+ * and wpe stay fp32. Accumulation is fp32 throughout. Decode steps of at most
+ * 16 sequences stream the compact copies (2 or 1 byte per element); every other
+ * path computes with the fp32 values the copies stand for, so the model is the
+ * same model whichever kernels run. A format's copies are built on the device
+ * on first selection and kept. */
+enum { TIE_WEIGHTS_F32 = 0, TIE_WEIGHTS_BF16 = 1, TIE_WEIGHTS_INT8 = 2 };
+model_status model_set_weight_format(model *m, int fmt);
+int model_weight_format(const model *m);
+
 /* The last CUDA failure behind a MODEL_ERR_DEVICE on the calling thread: the
  * error's name and text and the failing call, or "" if none yet. With the
  * environment variable TIE_DEBUG set, each such failure is also printed to

@@ -1,0 +1,85 @@
+"""The reduced weight formats (bf16, int8 per output channel).
+
+Parity: the engine running a format on the original weights must compute the
+same model as the fp32 engine running the weights that format stands for
+(written by tie_b200.synth.reduce_matrix: bf16 round-to-nearest-even; int8
+scale = absmax / 127, q = rint(w / scale) clamped, weight q * scale). The two
+differ only in summation order (and, for int8, the scale applied after the
+sum), so the logits agree to LOGIT_TOL.
+
+The error of each format against the fp32 weights is a property of the format,
+not a bug; it is measured here, printed, and held to the stated bounds below.
+"""
+import numpy as np
+import pytest
+
+import tie_b200
+from tie_b200 import synth
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-3
+FMTS = {"bf16": tie_b200.TIE_WEIGHTS_BF16, "int8": tie_b200.TIE_WEIGHTS_INT8}
+# stated error of the formats against fp32 weights (GPT-2 small, N(0, 0.02)
+# weights): max-abs logit difference over a 24-step greedy trace
+STATED_MAX_ABS = {"bf16": 0.05, "int8": 0.25}
+
+
+def _model(shape, seed, ln, fmt="f32"):
+    w, inv, cfg = synth.ensure_model(shape, seed=seed, ln_affine=ln, fmt=fmt)
+    return tie_b200.Model(w, inv, cfg)
+
+
+def _trace(m, prompts, feed):
+    """Prefill, then decode steps feeding the given tokens; logits per step."""
+    S, T = prompts.shape
+    m.batch_reserve(S, T + feed.shape[1] + 1)
+    _, pl = m.prefill_batch(prompts, want_logits=True)
+    out = [pl[:, -1]]
+    for k in range(feed.shape[1]):
+        _, lg = m.decode_step_batch(feed[:, k], want_logits=True)
+        out.append(lg)
+    return np.stack(out, 1)
+
+
+@pytest.mark.parametrize("fmt", sorted(FMTS))
+@pytest.mark.parametrize("shape,seed,ln,n_seq", [("mini", 7, "random", 3), ("small", 1234, "unit", 1),
+                                                 ("small", 1234, "unit", 5), ("small", 1234, "unit", 20)])
+def test_format_is_the_model_it_stands_for(fmt, shape, seed, ln, n_seq):
+    steps = 8
+    with _model(shape, seed, ln, fmt) as ref, _model(shape, seed, ln) as m:
+        m.set_weight_format(FMTS[fmt])
+        assert m.weight_format() == FMTS[fmt]
+        prompts = synth.prompt_ids(m.vocab, n_seq, 17, seed=60 + n_seq)
+        feed = synth.prompt_ids(m.vocab, n_seq, steps, seed=70 + n_seq)
+        want = _trace(ref, prompts, feed)
+        got = _trace(m, prompts, feed)
+        err = float(np.abs(got - want).max())
+        print(f"{fmt} {shape} x{n_seq}: max-abs vs its fp32 stand-in {err:.3g}")
+        assert err <= LOGIT_TOL, err
+
+
+@pytest.mark.parametrize("fmt", sorted(FMTS))
+def test_format_error_against_fp32(fmt):
+    """GPT-2 small, batch 1: logits of a greedy trace in the format against the
+    fp32 weights on the same fed tokens."""
+    with _model("small", 1234, "unit") as m:
+        prompts = synth.prompt_ids(m.vocab, 1, 32, seed=5)
+        m.batch_reserve(1, 32 + 25)
+        feed = m.generate_greedy(prompts, 24)[:, :24]
+        base = _trace(m, prompts, feed)
+        m.set_weight_format(FMTS[fmt])
+        got = _trace(m, prompts, feed)
+        err = float(np.abs(got - base).max())
+        agree = float((got.argmax(-1) == base.argmax(-1)).mean())
+        print(f"{fmt}: max-abs logit error {err:.3g}, top-1 agreement {agree:.3f}")
+        assert err <= STATED_MAX_ABS[fmt], err
+        m.set_weight_format(tie_b200.TIE_WEIGHTS_F32)
+        again = _trace(m, prompts, feed)
+        assert np.array_equal(again, base)
+
+
+def test_format_validation():
+    with _model("tiny", 7, "random") as m:
+        with pytest.raises(tie_b200.ModelError):
+            m.set_weight_format(3)
+        assert m.weight_format() == tie_b200.TIE_WEIGHTS_F32

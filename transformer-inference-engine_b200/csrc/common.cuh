@@ -206,14 +206,24 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
                                int* counters = nullptr);
 
 // Small-batch (<= 16 rows) decode matmuls with optional LayerNorm prologue
-// (ln_g non-NULL) and PDL chaining (k_decode.cu).
+// (ln_g non-NULL) and PDL chaining (k_decode.cu). Weights fp32 (W), or with wt
+// 1 / 2 the bf16 / int8 copy wq (int8 with per-row scales).
+enum WeightFormat : int { WF_F32 = 0, WF_BF16 = 1, WF_INT8 = 2 };
 cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
-                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st);
-int dec_head_blocks(int V, int K);
+                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st, int wt = WF_F32,
+                            const void* wq = nullptr, const float* scale = nullptr);
+int dec_head_blocks(int V, int K, int wt = WF_F32);
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
-                            int* part_idx, cudaStream_t st);
+                            int* part_idx, cudaStream_t st, int wt = WF_F32, const void* wq = nullptr,
+                            const float* scale = nullptr);
+
+// The reduced weight formats (k_quant.cu). bf16: q = rn(w); int8: per row,
+// scale = absmax / 127, q = clamp(rint(w / scale)). deq receives the weights
+// the formats stand for, in fp32.
+cudaError_t launch_to_bf16(const float* w, void* q, float* deq, size_t n, cudaStream_t st);
+cudaError_t launch_quant_rows(const float* w, void* q, float* scale, float* deq, int N, int K, cudaStream_t st);
 
 // Step bookkeeping for device-resident greedy generation: tokens[b] = next[b];
 // out[b * ld + *step] = next[b]; lens[b] += 1; (block 0 thread 0) *step += 1.

@@ -64,7 +64,9 @@ struct DecArgs {
     const float* ln_g;
     const float* ln_b;
     float eps;
-    const float* W;   // [N][K], K-major
+    const float* W;   // [N][K], K-major (fp32)
+    const void* Wq;   // [N][K] bf16 or int8 (reduced weight formats)
+    const float* scale;   // [N] int8 per-row scales
     const float* bias;
     float* y;         // [M][ldy]
     int ldy;
@@ -93,7 +95,23 @@ __device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
 // chunks c, c + 32, ... (four FMAs per chunk, in order), then an xor-butterfly
 // across lanes; the WS slice sums are added in slice order. The order depends
 // only on K, so results do not depend on the batch a sequence decodes in.
-template <int EPI, bool LN, int RPW, int WS, int CPL>
+// Weight formats: WT 0 fp32 (4 elements per 16-byte chunk), 1 bf16 (8), 2 int8
+// (16, times the row's scale after the sum). For the reduced formats the
+// elements of a chunk are added in element order against the matching
+// activations; everything else is as for fp32.
+template <int WT> constexpr int elems_per_chunk() { return WT == 0 ? 4 : (WT == 1 ? 8 : 16); }
+
+// element e of a 16-byte chunk of a reduced format
+template <int WT>
+__device__ __forceinline__ float chunk_elem(const float4& c, int e) {
+    const uint32_t w = __float_as_uint(e >> (WT == 1 ? 1 : 2) == 0 ? c.x
+                                        : e >> (WT == 1 ? 1 : 2) == 1 ? c.y
+                                        : e >> (WT == 1 ? 1 : 2) == 2 ? c.z : c.w);
+    if constexpr (WT == 1) return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+    else return (float)(int8_t)(w >> (8 * (e & 3)));
+}
+
+template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
 __global__ void __launch_bounds__(kWarps * 32)
 dec_gemv_kernel(DecArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][K] when LN
@@ -102,7 +120,8 @@ dec_gemv_kernel(DecArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = warp / WS, ks = warp % WS;
     const int row0 = (blockIdx.x * GROUPS + grp) * RPW;
-    const int K4 = a.K >> 2;
+    constexpr int EPC = elems_per_chunk<WT>();
+    const int K4 = a.K / EPC;                       // 16-byte chunks per row
     const int slice = (K4 + WS - 1) / WS;          // 16-byte chunks per slice
     const int c0 = ks * slice, c1 = min(K4, c0 + slice);
 
@@ -113,8 +132,13 @@ dec_gemv_kernel(DecArgs a) {
 #pragma unroll
         for (int u = 0; u < CPL; ++u) {
             const int c = c0 + u * 32 + lane;
-            w[r][u] = (row0 + r < a.N && c < c1) ? ld_stream(a.W + (size_t)(row0 + r) * a.K + 4 * c)
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            const bool in = row0 + r < a.N && c < c1;
+            if constexpr (WT == 0)
+                w[r][u] = in ? ld_stream(a.W + (size_t)(row0 + r) * a.K + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            else
+                w[r][u] = in ? ld_stream(reinterpret_cast<const float*>(
+                                   reinterpret_cast<const char*>(a.Wq) + ((size_t)(row0 + r) * K4 + c) * 16))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     pdl_trigger();
     pdl_wait();
@@ -142,16 +166,34 @@ dec_gemv_kernel(DecArgs a) {
 #pragma unroll
             for (int m = 0; m < kMaxRows; ++m) {
                 if (m < a.M) {
-                    const float4 xv = LN ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
-                                         : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
+                    if constexpr (WT == 0) {
+                        const float4 xv = LN ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
+                                             : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
 #pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        float t = acc[r][m];
-                        t = fmaf(w[r][u].x, xv.x, t);
-                        t = fmaf(w[r][u].y, xv.y, t);
-                        t = fmaf(w[r][u].z, xv.z, t);
-                        t = fmaf(w[r][u].w, xv.w, t);
-                        acc[r][m] = t;
+                        for (int r = 0; r < RPW; ++r) {
+                            float t = acc[r][m];
+                            t = fmaf(w[r][u].x, xv.x, t);
+                            t = fmaf(w[r][u].y, xv.y, t);
+                            t = fmaf(w[r][u].z, xv.z, t);
+                            t = fmaf(w[r][u].w, xv.w, t);
+                            acc[r][m] = t;
+                        }
+                    } else {
+#pragma unroll
+                        for (int q4 = 0; q4 < EPC / 4; ++q4) {
+                            const float* xp = X + (size_t)m * ldx + (size_t)c * EPC + 4 * q4;
+                            const float4 xv = LN ? *reinterpret_cast<const float4*>(xp)
+                                                 : __ldg(reinterpret_cast<const float4*>(xp));
+#pragma unroll
+                            for (int r = 0; r < RPW; ++r) {
+                                float t = acc[r][m];
+                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 0), xv.x, t);
+                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 1), xv.y, t);
+                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 2), xv.z, t);
+                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 3), xv.w, t);
+                                acc[r][m] = t;
+                            }
+                        }
                     }
                 }
             }
@@ -187,6 +229,7 @@ dec_gemv_kernel(DecArgs a) {
                 float sum = s_part[grp][0][r][m];
 #pragma unroll
                 for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
+                if constexpr (WT == 2) sum = sum * __ldg(a.scale + j);
                 float* yp = a.y + (size_t)m * a.ldy + j;
                 float v;
                 if constexpr (EPI == DEC_BIAS || EPI == DEC_QKV_KV) v = apply_epi<EPI_BIAS>(sum, a.bias, j, yp);
@@ -218,6 +261,7 @@ dec_gemv_kernel(DecArgs a) {
                     if (j >= a.N) continue;
                     float v = s_part[g][0][r][m];
                     for (int k = 1; k < WS; ++k) v += s_part[g][k][r][m];
+                    if constexpr (WT == 2) v = v * __ldg(a.scale + j);
                     if (a.y) a.y[(size_t)m * a.ldy + j] = v;
                     if (j == 0 && !(v == v)) nan0 = true;
                     else if (v == v && beats(v, j, bv, bi)) { bv = v; bi = j; }
@@ -228,10 +272,10 @@ dec_gemv_kernel(DecArgs a) {
     }
 }
 
-template <int EPI, bool LN, int RPW, int WS, int CPL>
+template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
 cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
     const size_t smem = LN ? (size_t)a.M * a.K * sizeof(float) : 0;
-    auto k = dec_gemv_kernel<EPI, LN, RPW, WS, CPL>;
+    auto k = dec_gemv_kernel<EPI, LN, RPW, WS, CPL, WT>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -243,65 +287,90 @@ cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
 }
 
 // The slicing of K for a matrix: each lane holds at most 8 chunks per row.
-//   K <= 1024 (K4 <= 256): whole rows, WS = 1
-//   K <= 4096: WS = 4; K <= 8192: WS = 4 with 16 chunks per lane
-template <int EPI, bool LN>
+//   at most 256 chunks per row: whole rows, WS = 1
+//   at most 1024: WS = 4; at most 2048 (fp32 only): WS = 4 with 16 chunks per lane
+template <int EPI, bool LN, int WT>
 cudaError_t dec_dispatch(const DecArgs& a, cudaStream_t st) {
-    const int K4 = a.K >> 2;
-    if (K4 <= 256) return dec_launch<EPI, LN, 1, 1, 8>(a, st);
-    if (K4 <= 1024) return dec_launch<EPI, LN, 1, 4, 8>(a, st);
-    if (K4 <= 2048) return dec_launch<EPI, LN, 1, 4, 16>(a, st);
+    const int KC = a.K / elems_per_chunk<WT>();
+    if (KC <= 256) return dec_launch<EPI, LN, 1, 1, 8, WT>(a, st);
+    if (KC <= 1024) return dec_launch<EPI, LN, 1, 4, 8, WT>(a, st);
+    if constexpr (WT == 0)
+        if (KC <= 2048) return dec_launch<EPI, LN, 1, 4, 16, WT>(a, st);
     return cudaErrorInvalidValue;
 }
+
+template <int EPI, int WT>
+cudaError_t dec_dispatch_ln(const DecArgs& a, bool ln, cudaStream_t st) {
+    return ln ? dec_dispatch<EPI, true, WT>(a, st) : dec_dispatch<EPI, false, WT>(a, st);
+}
+
+template <int WT>
+cudaError_t dec_dispatch_epi(const DecArgs& a, int epi, bool ln, cudaStream_t st) {
+    switch (epi) {
+        case EPI_BIAS: return dec_dispatch_ln<DEC_BIAS, WT>(a, ln, st);
+        case EPI_BIAS_GELU: return dec_dispatch_ln<DEC_BIAS_GELU, WT>(a, ln, st);
+        case EPI_BIAS_RESID: return dec_dispatch_ln<DEC_BIAS_RESID, WT>(a, ln, st);
+        case EPI_QKV_KV: return dec_dispatch_ln<DEC_QKV_KV, WT>(a, ln, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int WT>
+cudaError_t head_dispatch(const DecArgs& a, bool ln, cudaStream_t st) {
+    const int KC = a.K / elems_per_chunk<WT>();
+    if (KC <= 256)
+        return ln ? dec_launch<DEC_HEAD, true, 4, 1, 8, WT>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8, WT>(a, st);
+    if (KC <= 1024)
+        return ln ? dec_launch<DEC_HEAD, true, 1, 4, 8, WT>(a, st) : dec_launch<DEC_HEAD, false, 1, 4, 8, WT>(a, st);
+    return cudaErrorInvalidValue;
+}
+
+int chunk_elems(int wt) { return wt == 0 ? 4 : (wt == 1 ? 8 : 16); }
 
 }  // namespace
 
 // Rows per head block: 4 rows in each of 4 warps while a row is at most 256
 // chunks (RPW 4, WS 1), else one row cut into 4 slices (RPW 1, WS 4).
-int dec_head_blocks(int V, int K) {
-    const int rows = (K >> 2) <= 256 ? kWarps * 4 : 1;
+int dec_head_blocks(int V, int K, int wt) {
+    const int rows = K / chunk_elems(wt) <= 256 ? kWarps * 4 : 1;
     return (V + rows - 1) / rows;
 }
 
-// y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL.
+// y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL. Weights
+// fp32 (W), or with wt 1 / 2 bf16 / int8 (wq, int8 with per-row scales).
 cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
-                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st) {
-    if (M <= 0 || M > kMaxRows || (K & 3) || (ldx & 3)) return cudaErrorInvalidValue;
+                            int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st, int wt,
+                            const void* wq, const float* scale) {
+    if (M <= 0 || M > kMaxRows || (ldx & 3) || wt < 0 || wt > 2 || K % chunk_elems(wt)) return cudaErrorInvalidValue;
+    if ((wt != 0 && !wq) || (wt == 2 && !scale)) return cudaErrorInvalidValue;
+    if (epi == EPI_QKV_KV && (!kv || !lens)) return cudaErrorInvalidValue;
     DecArgs a{};
     a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W; a.bias = bias;
+    a.Wq = wq; a.scale = scale;
     a.y = y; a.ldy = ldy; a.M = M; a.N = N; a.K = K;
     if (kv) a.kv = *kv;
     a.lens = lens;
     const bool ln = ln_g != nullptr;
-    switch (epi) {
-        case EPI_BIAS: return ln ? dec_dispatch<DEC_BIAS, true>(a, st) : dec_dispatch<DEC_BIAS, false>(a, st);
-        case EPI_BIAS_GELU:
-            return ln ? dec_dispatch<DEC_BIAS_GELU, true>(a, st) : dec_dispatch<DEC_BIAS_GELU, false>(a, st);
-        case EPI_BIAS_RESID:
-            return ln ? dec_dispatch<DEC_BIAS_RESID, true>(a, st) : dec_dispatch<DEC_BIAS_RESID, false>(a, st);
-        case EPI_QKV_KV:
-            if (!kv || !lens) return cudaErrorInvalidValue;
-            return ln ? dec_dispatch<DEC_QKV_KV, true>(a, st) : dec_dispatch<DEC_QKV_KV, false>(a, st);
-    }
-    return cudaErrorInvalidValue;
+    if (wt == 1) return dec_dispatch_epi<1>(a, epi, ln, st);
+    if (wt == 2) return dec_dispatch_epi<2>(a, epi, ln, st);
+    return dec_dispatch_epi<0>(a, epi, ln, st);
 }
 
 // The tied head with LN_f in its prologue: logits (optional) and per-block
 // partial maxima for launch_argmax_finalize.
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
-                            int* part_idx, cudaStream_t st) {
-    if (M <= 0 || M > kMaxRows || (K & 3) || (ldx & 3)) return cudaErrorInvalidValue;
+                            int* part_idx, cudaStream_t st, int wt, const void* wq, const float* scale) {
+    if (M <= 0 || M > kMaxRows || (ldx & 3) || wt < 0 || wt > 2 || K % chunk_elems(wt)) return cudaErrorInvalidValue;
+    if ((wt != 0 && !wq) || (wt == 2 && !scale)) return cudaErrorInvalidValue;
     DecArgs a{};
-    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W;
+    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W; a.Wq = wq; a.scale = scale;
     a.y = logits; a.ldy = ldl; a.M = M; a.N = V; a.K = K; a.part_val = part_val; a.part_idx = part_idx;
-    const int K4 = K >> 2;
-    if (K4 <= 256)
-        return ln_g ? dec_launch<DEC_HEAD, true, 4, 1, 8>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8>(a, st);
-    if (K4 <= 1024)
-        return ln_g ? dec_launch<DEC_HEAD, true, 1, 4, 8>(a, st) : dec_launch<DEC_HEAD, false, 1, 4, 8>(a, st);
-    return cudaErrorInvalidValue;
+    const bool ln = ln_g != nullptr;
+    if (wt == 1) return head_dispatch<1>(a, ln, st);
+    if (wt == 2) return head_dispatch<2>(a, ln, st);
+    return head_dispatch<0>(a, ln, st);
 }
 
 }  // namespace tie

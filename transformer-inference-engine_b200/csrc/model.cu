@@ -139,6 +139,25 @@ struct Layer {
     float *qkv_hi, *qkv_lo, *proj_hi, *proj_lo, *fc_hi, *fc_lo, *mlp_hi, *mlp_lo;
 };
 
+// A reduced-format matrix as the small-batch decode streams it.
+struct QMat {
+    int wt = WF_F32;              // WF_BF16 or WF_INT8 (WF_F32: use the fp32 weights)
+    const void* q = nullptr;      // [out][in] bf16 or int8
+    const float* s = nullptr;     // [out] int8 scales
+};
+
+// One reduced weight format (k_quant.cu): the compact copies of the five
+// matrix kinds (qkv, proj, fc, mlp per layer; the tied wte) and the fp32
+// weights they stand for, with their tf32 splits, which every other path uses
+// while the format is selected. Vectors (LayerNorm, biases) and wpe stay fp32.
+struct WeightSet {
+    void* block = nullptr;
+    size_t bytes = 0;
+    std::vector<Layer> layers;    // fp32 view: the dequantised matrices
+    float *wte = nullptr, *wte_hi = nullptr, *wte_lo = nullptr;
+    std::vector<QMat> q;          // per layer: qkv, proj, fc, mlp; then wte
+};
+
 // A matmul operand: its fp32 values and/or its tf32 split.
 struct Mat {
     const float* f;
@@ -187,8 +206,13 @@ struct model {
     size_t split_bytes = 0;
     float *wte = nullptr, *wpe = nullptr, *lnf_w = nullptr, *lnf_b = nullptr;
     float *wte_hi = nullptr, *wte_lo = nullptr;
-    std::vector<Layer> layers;
+    std::vector<Layer> layers;        // the selected weight format's fp32 view
     std::vector<model_tensor_record> records;
+    // the weights as loaded, and the reduced formats built on request
+    int wfmt = WF_F32;
+    std::vector<Layer> base_layers;
+    float *base_wte = nullptr, *base_wte_hi = nullptr, *base_wte_lo = nullptr;
+    WeightSet sets[3];
 
     // activation scratch: `rows` rows
     size_t rows = 0;
@@ -479,6 +503,77 @@ model_status prefill_head(model* m, int rows, size_t first, int stride) {
 // m->logits [B, V] and the greedy choice into d_next.          model.c:794-868
 // Everything it reads from the host side is fixed at capture time, so the
 // sequence can be recorded once and replayed as a graph.
+// The compact copy of matrix `which` (0 qkv, 1 proj, 2 fc, 3 mlp) of layer l
+// in the selected format; layer n_layer, which 0, is the tied head.
+QMat qmat(const model* m, int l, int which) {
+    if (m->wfmt == WF_F32) return QMat{};
+    const WeightSet& s = m->sets[m->wfmt];
+    return l == m->cfg.n_layer ? s.q.back() : s.q[(size_t)l * 4 + which];
+}
+
+// Builds weight format `fmt` from the loaded fp32 weights (once).
+model_status build_weight_set(model* m, int fmt) {
+    WeightSet& set = m->sets[fmt];
+    if (set.block) return MODEL_OK;
+    const size_t E = (size_t)m->cfg.n_embd, V = (size_t)m->cfg.vocab_size, L = (size_t)m->cfg.n_layer;
+    struct Mtx { const float* src; size_t N, K; };
+    std::vector<Mtx> mats;
+    for (const Layer& y : m->base_layers) {
+        mats.push_back({y.qkv_w, 3 * E, E});
+        mats.push_back({y.proj_w, E, E});
+        mats.push_back({y.fc_w, 4 * E, E});
+        mats.push_back({y.mlp_w, E, 4 * E});
+    }
+    mats.push_back({m->base_wte, V, E});
+    auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    size_t bytes = 0;
+    for (const Mtx& x : mats) {
+        const size_t n = x.N * x.K;
+        bytes += 3 * up(n * 4) + up(n * (fmt == WF_BF16 ? 2 : 1)) + (fmt == WF_INT8 ? up(x.N * 4) : 0);
+    }
+    char* block = nullptr;
+    if (cudaMalloc(&block, bytes) != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_NOMEM; }
+    char* cur = block;
+    auto take = [&](size_t b) { char* p = cur; cur += up(b); return p; };
+    std::vector<QMat> q;
+    std::vector<float*> deq, hi, lo;
+    cudaError_t e = cudaSuccess;
+    for (const Mtx& x : mats) {
+        const size_t n = x.N * x.K;
+        float* d = reinterpret_cast<float*>(take(n * 4));
+        float* h = reinterpret_cast<float*>(take(n * 4));
+        float* o = reinterpret_cast<float*>(take(n * 4));
+        void* c = take(n * (fmt == WF_BF16 ? 2 : 1));
+        float* sc = fmt == WF_INT8 ? reinterpret_cast<float*>(take(x.N * 4)) : nullptr;
+        if (e == cudaSuccess)
+            e = fmt == WF_BF16 ? launch_to_bf16(x.src, c, d, n, m->st)
+                               : launch_quant_rows(x.src, c, sc, d, (int)x.N, (int)x.K, m->st);
+        if (e == cudaSuccess) e = launch_split_hilo(d, h, o, (long long)n, m->st);
+        q.push_back(QMat{fmt, c, sc});
+        deq.push_back(d); hi.push_back(h); lo.push_back(o);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+    if (e != cudaSuccess) {
+        note_cuda(e, "building a reduced weight format", __LINE__);
+        cudaGetLastError();
+        cudaFree(block);
+        return MODEL_ERR_DEVICE;
+    }
+    set.block = block;
+    set.bytes = bytes;
+    set.q = q;
+    set.layers = m->base_layers;
+    for (size_t l = 0; l < L; ++l) {
+        Layer& y = set.layers[l];
+        y.qkv_w = deq[4 * l]; y.qkv_hi = hi[4 * l]; y.qkv_lo = lo[4 * l];
+        y.proj_w = deq[4 * l + 1]; y.proj_hi = hi[4 * l + 1]; y.proj_lo = lo[4 * l + 1];
+        y.fc_w = deq[4 * l + 2]; y.fc_hi = hi[4 * l + 2]; y.fc_lo = lo[4 * l + 2];
+        y.mlp_w = deq[4 * l + 3]; y.mlp_hi = hi[4 * l + 3]; y.mlp_lo = lo[4 * l + 3];
+    }
+    set.wte = deq.back(); set.wte_hi = hi.back(); set.wte_lo = lo.back();
+    return MODEL_OK;
+}
+
 model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
     const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size;
     const float eps = m->cfg.layer_norm_epsilon;
@@ -498,22 +593,24 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
         // fused, PDL-chained kernels: 5 per layer (k_decode.cu)
         for (int l = 0; l < m->cfg.n_layer; ++l) {
             const Layer& w = m->layers[l];
+            const QMat q0 = qmat(m, l, 0), q1 = qmat(m, l, 1), q2 = qmat(m, l, 2), q3 = qmat(m, l, 3);
             const PagedKV view = layer_view(cache, l);
             LAUNCH(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, eps, w.qkv_w, w.qkv_b, m->qkv, 3 * E, B, 3 * E, E,
-                                   EPI_QKV_KV, &view, m->d_lens, st));
+                                   EPI_QKV_KV, &view, m->d_lens, st, q0.wt, q0.q, q0.s));
             LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st,
                                       nullptr, nullptr, m->d_attn_cnt));
             if (stats) ++m->launches;  // the separate merge kernel
             LAUNCH(launch_dec_gemv(m->attn, E, nullptr, nullptr, eps, w.proj_w, w.proj_b, m->x, E, B, E, E,
-                                   EPI_BIAS_RESID, nullptr, nullptr, st));
+                                   EPI_BIAS_RESID, nullptr, nullptr, st, q1.wt, q1.q, q1.s));
             LAUNCH(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, eps, w.fc_w, w.fc_b, m->ff, 4 * E, B, 4 * E, E,
-                                   EPI_BIAS_GELU, nullptr, nullptr, st));
+                                   EPI_BIAS_GELU, nullptr, nullptr, st, q2.wt, q2.q, q2.s));
             LAUNCH(launch_dec_gemv(m->ff, 4 * E, nullptr, nullptr, eps, w.mlp_w, w.mlp_b, m->x, E, B, E, 4 * E,
-                                   EPI_BIAS_RESID, nullptr, nullptr, st));
+                                   EPI_BIAS_RESID, nullptr, nullptr, st, q3.wt, q3.q, q3.s));
         }
+        const QMat qh = qmat(m, m->cfg.n_layer, 0);
         LAUNCH(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
-                               m->d_am_idx, st));
-        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E), B, m->d_next, st));
+                               m->d_am_idx, st, qh.wt, qh.q, qh.s));
+        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, qh.wt), B, m->d_next, st));
         if (advance)
             LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
         return MODEL_OK;
@@ -553,7 +650,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
 // Whether a step of B sequences takes the persistent kernel; allocates its
 // layer table and counters on first use.
 bool use_step(model* m, int B, const kv_cache* cache) {
-    if (m->step_kind != TIE_STEP_PERSISTENT || m->stats_on || B < 1 || B > 4) return false;
+    if (m->step_kind != TIE_STEP_PERSISTENT || m->stats_on || m->wfmt != WF_F32 || B < 1 || B > 4) return false;
     if (!cache || cache->pages_per_seq > step_max_pages()) return false;
     int& state = m->step_state[B];
     if (state == 0) {
@@ -924,6 +1021,8 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
                 TRY(split(y.fc_w, 4 * E * E, &y.fc_hi, &y.fc_lo));
                 TRY(split(y.mlp_w, 4 * E * E, &y.mlp_hi, &y.mlp_lo));
             }
+            m->base_layers = m->layers;
+            m->base_wte = m->wte; m->base_wte_hi = m->wte_hi; m->base_wte_lo = m->wte_lo;
             if (cudaDeviceSynchronize() != cudaSuccess) {
                 cudaGetLastError();
                 rc = MODEL_ERR_DEVICE;
@@ -995,6 +1094,7 @@ void model_free(model* m) {
     cudaFree(m->d_out); cudaFree(m->d_part); cudaFree(m->d_attn_cnt); cudaFree(m->d_am_val); cudaFree(m->d_am_idx);
     cudaFree(m->d_stats);
     cudaFree(m->d_step_layers); cudaFree(m->d_sync);
+    cudaFree(m->sets[1].block); cudaFree(m->sets[2].block);
     if (m->h_small) cudaFreeHost(m->h_small);
     kv_cache_destroy(m->kv);
     kv_cache_destroy(m->pool);
@@ -1196,7 +1296,9 @@ model_status model_decode_step(model* m, const int32_t* ids, size_t T, float* lo
 // ----------------------------------------------------------------- batches --
 int model_device(const model* m) { return m ? m->device : -1; }
 void* model_stream(const model* m) { return m ? (void*)m->st : nullptr; }
-size_t model_weight_device_bytes(const model* m) { return m ? m->weight_bytes + m->split_bytes : 0; }
+size_t model_weight_device_bytes(const model* m) {
+    return m ? m->weight_bytes + m->split_bytes + m->sets[1].bytes + m->sets[2].bytes : 0;
+}
 uint64_t model_kernel_launches(const model* m) { return m ? m->launches : 0; }
 
 model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
@@ -1361,6 +1463,29 @@ model_status model_step_trace(model* m, size_t rows, size_t context, uint64_t* o
     return rc;
 }
 
+model_status model_set_weight_format(model* m, int fmt) {
+    if (!m || fmt < TIE_WEIGHTS_F32 || fmt > TIE_WEIGHTS_INT8) return MODEL_ERR_ARG;
+    if (fmt == m->wfmt) return MODEL_OK;
+    if (fmt != WF_F32) {
+        model_status rc = build_weight_set(m, fmt);
+        if (rc != MODEL_OK) return rc;
+    }
+    CU(cudaStreamSynchronize(m->st));
+    drop_graphs(m);
+    if (fmt == WF_F32) {
+        m->layers = m->base_layers;
+        m->wte = m->base_wte; m->wte_hi = m->base_wte_hi; m->wte_lo = m->base_wte_lo;
+    } else {
+        const WeightSet& s = m->sets[fmt];
+        m->layers = s.layers;
+        m->wte = s.wte; m->wte_hi = s.wte_hi; m->wte_lo = s.wte_lo;
+    }
+    m->wfmt = fmt;
+    return MODEL_OK;
+}
+
+int model_weight_format(const model* m) { return m ? m->wfmt : -1; }
+
 model_status model_set_step_kernel(model* m, int kind) {
     if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED)) return MODEL_ERR_ARG;
     if (kind != m->step_kind) drop_graphs(m);
@@ -1404,33 +1529,38 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                 return MODEL_OK;
             case TIE_KERNEL_DECODE_QKV:
                 if (small) {
+                    const QMat q = qmat(m, 0, 0);
                     CU(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, m->cfg.layer_norm_epsilon, w.qkv_w, w.qkv_b, m->qkv,
-                                       3 * E, B, 3 * E, E, EPI_QKV_KV, &view, m->d_lens, st));
+                                       3 * E, B, 3 * E, E, EPI_QKV_KV, &view, m->d_lens, st, q.wt, q.q, q.s));
                     return MODEL_OK;
                 }
                 return matmul(m, true, B, xb, E, Mat{w.qkv_w, w.qkv_hi, w.qkv_lo}, 3 * E, E, w.qkv_b, EPI_BIAS,
                               m->qkv, nullptr, nullptr, 3 * E);
             case TIE_KERNEL_DECODE_FC:
                 if (small) {
+                    const QMat q = qmat(m, 0, 2);
                     CU(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, m->cfg.layer_norm_epsilon, w.fc_w, w.fc_b, m->ff,
-                                       4 * E, B, 4 * E, E, EPI_BIAS_GELU, nullptr, nullptr, st));
+                                       4 * E, B, 4 * E, E, EPI_BIAS_GELU, nullptr, nullptr, st, q.wt, q.q, q.s));
                     return MODEL_OK;
                 }
                 return matmul(m, true, B, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b, EPI_BIAS_GELU,
                               nullptr, m->ff_hi, m->ff_lo, 4 * E);
             case TIE_KERNEL_DECODE_MLP_PROJ:
                 if (small) {
+                    const QMat q = qmat(m, 0, 3);
                     CU(launch_dec_gemv(m->ff, 4 * E, nullptr, nullptr, 0.f, w.mlp_w, w.mlp_b, m->x, E, B, E, 4 * E,
-                                       EPI_BIAS_RESID, nullptr, nullptr, st));
+                                       EPI_BIAS_RESID, nullptr, nullptr, st, q.wt, q.q, q.s));
                     return MODEL_OK;
                 }
                 return matmul(m, true, B, ff, 4 * E, Mat{w.mlp_w, w.mlp_hi, w.mlp_lo}, E, 4 * E, w.mlp_b,
                               EPI_BIAS_RESID, m->x, nullptr, nullptr, E);
             case TIE_KERNEL_DECODE_HEAD:
                 if (small) {
+                    const QMat q = qmat(m, m->cfg.n_layer, 0);
                     CU(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, m->cfg.layer_norm_epsilon, m->wte, m->logits, V,
-                                       B, V, E, m->d_am_val, m->d_am_idx, st));
-                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E), B, m->d_next, st));
+                                       B, V, E, m->d_am_val, m->d_am_idx, st, q.wt, q.q, q.s));
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, q.wt), B, m->d_next,
+                                              st));
                     return MODEL_OK;
                 } else {
                     model_status r = matmul(m, true, B, xb, E, Mat{m->wte, m->wte_hi, m->wte_lo}, V, E, nullptr,

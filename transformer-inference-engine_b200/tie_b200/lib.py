@@ -20,6 +20,7 @@ for _i, _n in enumerate(MODEL_STATUS + KV_STATUS):
     globals()[_n] = _i if _n in MODEL_STATUS else KV_STATUS.index(_n)
 MODEL_PATH_NOCACHE, MODEL_PATH_CACHE = 0, 1
 TIE_STEP_PERSISTENT, TIE_STEP_CHAINED = 0, 1
+TIE_WEIGHTS_F32, TIE_WEIGHTS_BF16, TIE_WEIGHTS_INT8 = 0, 1, 2
 MODEL_CPROJ_AS_STORED, MODEL_CPROJ_TRANSPOSED = 0, 1
 
 _fp = C.POINTER(C.c_float)
@@ -118,6 +119,8 @@ def library():
         "model_generate_greedy_device": (C.c_int, [_vp, _vp, C.c_size_t, C.c_size_t, C.c_size_t, _vp]),
         "model_time_kernel": (C.c_int, [_vp, C.c_int, C.c_size_t, C.c_size_t, C.c_int, _fp]),
         "model_set_step_kernel": (C.c_int, [_vp, C.c_int]),
+        "model_set_weight_format": (C.c_int, [_vp, C.c_int]),
+        "model_weight_format": (C.c_int, [_vp]),
         "model_step_trace": (C.c_int, [_vp, C.c_size_t, C.c_size_t, _vp, C.c_size_t,
                                        C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
         "tie_last_device_error": (C.c_char_p, []),
@@ -280,6 +283,13 @@ class Model:
 
     def set_decode_path(self, p):
         library().model_set_decode_path(self.h, p)
+
+    def set_weight_format(self, fmt):
+        """TIE_WEIGHTS_F32 (default), TIE_WEIGHTS_BF16 or TIE_WEIGHTS_INT8."""
+        _chk(library().model_set_weight_format(self.h, fmt), "model_set_weight_format")
+
+    def weight_format(self):
+        return library().model_weight_format(self.h)
 
     def set_step_kernel(self, kind):
         """TIE_STEP_PERSISTENT (default) or TIE_STEP_CHAINED for decode steps of <= 4 sequences."""

@@ -119,9 +119,46 @@ def _orientation(name: str, shape, s: GPT2Shape):
             f"and extent 1 is n_embd = {shape[1]}: one row per index.")
 
 
-def write_model(out_dir: str, s: GPT2Shape, seed: int = 1234, ln_affine: str = "unit"):
+def bf16_round(w: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even) -> fp32, for finite values."""
+    u = np.ascontiguousarray(w, dtype=np.float32).view(np.uint32)
+    r = ((u >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    return ((u + r) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def int8_dequant(w: np.ndarray, axis: int) -> np.ndarray:
+    """Per-channel symmetric absmax int8 of w, reduced along `axis` (the input
+    axis), back to fp32: scale = absmax / 127, q = rint(w / scale) clamped to
+    +-127 (0 for an all-zero channel), weight = q * scale -- all in fp32."""
+    w = np.asarray(w, dtype=np.float32)
+    scale = (np.max(np.abs(w), axis=axis, keepdims=True) / np.float32(127)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(scale > 0, np.rint(w / scale), np.float32(0)).astype(np.float32)
+    q = np.clip(q, -127, 127).astype(np.float32)
+    return (q * scale).astype(np.float32)
+
+
+def reduce_matrix(name: str, w: np.ndarray, fmt: str) -> np.ndarray:
+    """The weight a reduced format stands for, for one tensor as stored in the
+    file: the five matrix kinds are reduced (wte per row; the layers' [input,
+    output] matrices per output column), everything else is left as is."""
+    if fmt == "f32":
+        return w
+    is_matrix = name == "wte.weight" or (name.startswith("h.") and name.endswith(".weight") and w.ndim == 2)
+    if not is_matrix:
+        return w
+    if fmt == "bf16":
+        return bf16_round(w)
+    if fmt == "int8":
+        return int8_dequant(w, axis=1 if name == "wte.weight" else 0)
+    raise ValueError(fmt)
+
+
+def write_model(out_dir: str, s: GPT2Shape, seed: int = 1234, ln_affine: str = "unit", fmt: str = "f32"):
     """Writes model.safetensors, config.json and inventory.json into out_dir.
-    Returns the three paths (weights, inventory, config)."""
+    With fmt "bf16" or "int8" the matrices are the fp32 weights that reduced
+    format stands for (reduce_matrix). Returns the three paths (weights,
+    inventory, config)."""
     os.makedirs(out_dir, exist_ok=True)
     specs = tensor_specs(s)
     offsets, header = [], {"__metadata__": {"format": "pt"}}
@@ -141,7 +178,8 @@ def write_model(out_dir: str, s: GPT2Shape, seed: int = 1234, ln_affine: str = "
         f.write(struct.pack("<Q", len(hdr)))
         f.write(hdr)
         for idx, (name, shape, kind) in enumerate(specs):
-            f.write(_draw(kind, shape, seed, idx, ln_affine).astype("<f4").tobytes())
+            w = _draw(kind, shape, seed, idx, ln_affine).reshape(shape)
+            f.write(reduce_matrix(name, w, fmt).astype("<f4").tobytes())
     os.replace(tmp, wpath)
 
     cpath = os.path.join(out_dir, "config.json")
@@ -191,16 +229,19 @@ def default_cache_dir() -> str:
     return os.environ.get("TIE_CACHE_DIR", os.path.join(root, "_cache"))
 
 
-def ensure_model(shape: str, seed: int = 1234, ln_affine: str = "unit", cache_dir: str | None = None):
+def ensure_model(shape: str, seed: int = 1234, ln_affine: str = "unit", cache_dir: str | None = None,
+                 fmt: str = "f32"):
     """Returns (weights, inventory, config) for a named shape, writing them once
-    into the cache directory (keyed by shape, seed and LayerNorm init)."""
+    into the cache directory (keyed by shape, seed, LayerNorm init and, for a
+    reduced-format stand-in, the format)."""
     s = SHAPES[shape]
-    d = os.path.join(cache_dir or default_cache_dir(), f"{shape}_s{seed}_{ln_affine}")
+    tag = "" if fmt == "f32" else f"_{fmt}"
+    d = os.path.join(cache_dir or default_cache_dir(), f"{shape}_s{seed}_{ln_affine}{tag}")
     paths = (os.path.join(d, "model.safetensors"), os.path.join(d, "inventory.json"),
              os.path.join(d, "config.json"))
     if all(os.path.exists(p) for p in paths):
         return paths
-    return write_model(d, s, seed=seed, ln_affine=ln_affine)
+    return write_model(d, s, seed=seed, ln_affine=ln_affine, fmt=fmt)
 
 
 def prompt_ids(vocab_size: int, n_seq: int, n_tokens: int, seed: int) -> np.ndarray:
