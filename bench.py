@@ -71,6 +71,9 @@ def parse():
     p.add_argument("--rows", type=int, default=128)
     p.add_argument("--context", type=int, default=256)
     p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--shape", default="small", choices=["small", "medium", "xl"],
+                   help="model of the --kernel mode")
+    p.add_argument("--fmt", default="f32", choices=["f32", "bf16", "int8"], help="weight format of the --kernel mode")
     return p.parse_args()
 
 
@@ -435,13 +438,16 @@ def run_ours(args, rank, local_rank, world):
 
 
 def run_kernel(args):
-    """One kernel of the GPT-2 small forward pass, alone, at (rows, context)."""
+    """One kernel of a GPT-2 forward pass, alone, at (rows, context)."""
     import tie_b200
-    w, inv, cfg = synth.ensure_model("small", seed=WEIGHT_SEED)
+    w, inv, cfg = synth.ensure_model(args.shape, seed=WEIGHT_SEED)
     m = tie_b200.Model(w, inv, cfg, device=0)
+    if args.fmt != "f32":
+        m.set_weight_format({"bf16": tie_b200.TIE_WEIGHTS_BF16, "int8": tie_b200.TIE_WEIGHTS_INT8}[args.fmt])
     m.batch_reserve(args.rows, args.context)
     ms = m.time_kernel(args.kernel, args.rows, args.context, iters=args.iters)
-    print(json.dumps({"kernel": args.kernel, "rows": args.rows, "context": args.context,
+    print(json.dumps({"kernel": args.kernel, "shape": args.shape, "fmt": args.fmt, "rows": args.rows,
+                      "context": args.context,
                       "iters": args.iters, "ms_per_launch": ms}), flush=True)
     m.close()
     return 0

@@ -25,6 +25,7 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kMaxRows = 16;
+constexpr int kStageFloats = 0;               // activation rows copied to shared memory up to this many floats (0: read through L1)
 
 __device__ __forceinline__ float4 ld_stream(const float* p) {
     float4 v;
@@ -104,184 +105,254 @@ template <int WT> constexpr int elems_per_chunk() { return WT == 0 ? 4 : (WT == 
 // element e of a 16-byte chunk of a reduced format
 template <int WT>
 __device__ __forceinline__ float chunk_elem(const float4& c, int e) {
+    if constexpr (WT == 0) return e == 0 ? c.x : e == 1 ? c.y : e == 2 ? c.z : c.w;
+    else {
     const uint32_t w = __float_as_uint(e >> (WT == 1 ? 1 : 2) == 0 ? c.x
                                         : e >> (WT == 1 ? 1 : 2) == 1 ? c.y
                                         : e >> (WT == 1 ? 1 : 2) == 2 ? c.z : c.w);
     if constexpr (WT == 1) return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
     else return (float)(int8_t)(w >> (8 * (e & 3)));
+    }
 }
 
+// The kernel is persistent: a block normalises (or stages) the activation
+// rows once and then walks row groups blockIdx.x, + gridDim.x, ... The first
+// group's weights are loaded before the dependency wait; each later group's
+// are loaded while the previous group's sums are finished.
 template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
 __global__ void __launch_bounds__(kWarps * 32)
 dec_gemv_kernel(DecArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][K] when LN
     constexpr int GROUPS = kWarps / WS;          // row groups per block
+    constexpr int RPB = GROUPS * RPW;            // rows per block iteration
     __shared__ float s_part[GROUPS][WS][RPW][kMaxRows];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = warp / WS, ks = warp % WS;
-    const int row0 = (blockIdx.x * GROUPS + grp) * RPW;
     constexpr int EPC = elems_per_chunk<WT>();
     const int K4 = a.K / EPC;                       // 16-byte chunks per row
     const int slice = (K4 + WS - 1) / WS;          // 16-byte chunks per slice
     const int c0 = ks * slice, c1 = min(K4, c0 + slice);
+    const int n_iter_rows = a.N;
 
-    // 1. every weight chunk of this warp, before the dependency wait
+    // this warp's weight chunks of one row group (registers)
     float4 w[RPW][CPL];
+    auto load = [&](int row0) {
 #pragma unroll
-    for (int r = 0; r < RPW; ++r)
+        for (int r = 0; r < RPW; ++r)
 #pragma unroll
-        for (int u = 0; u < CPL; ++u) {
-            const int c = c0 + u * 32 + lane;
-            const bool in = row0 + r < a.N && c < c1;
-            if constexpr (WT == 0)
-                w[r][u] = in ? ld_stream(a.W + (size_t)(row0 + r) * a.K + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            else
-                w[r][u] = in ? ld_stream(reinterpret_cast<const float*>(
-                                   reinterpret_cast<const char*>(a.Wq) + ((size_t)(row0 + r) * K4 + c) * 16))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+            for (int u = 0; u < CPL; ++u) {
+                const int c = c0 + u * 32 + lane;
+                const bool in = row0 + r < a.N && c < c1;
+                if constexpr (WT == 0)
+                    w[r][u] = in ? ld_stream(a.W + (size_t)(row0 + r) * a.K + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                else
+                    w[r][u] = in ? ld_stream(reinterpret_cast<const float*>(
+                                       reinterpret_cast<const char*>(a.Wq) + ((size_t)(row0 + r) * K4 + c) * 16))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+    };
+
+    // 1. the first group's weights, before the dependency wait
+    load((blockIdx.x * GROUPS + grp) * RPW);
     pdl_trigger();
     pdl_wait();
 
-    // 2. the activation rows
+    // 2. the activation rows, once per block: normalised into shared memory,
+    //    or copied there when they fit (kStageFloats), else read through L1
     const float* X = a.x;
     int ldx = a.ldx;
+    const bool staged = LN || a.M * a.K <= kStageFloats;
     if constexpr (LN) {
         ln_rows_to_smem(a.x, a.ldx, a.ln_g, a.ln_b, a.eps, a.M, a.K, xs);
         __syncthreads();
         X = xs;
         ldx = a.K;
+    } else if (staged) {
+        const int K4x = a.K >> 2;
+        for (int i = threadIdx.x; i < a.M * K4x; i += kWarps * 32) {
+            const int m = i / K4x, c = i - m * K4x;
+            reinterpret_cast<float4*>(xs + (size_t)m * a.K)[c] =
+                __ldg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx) + c);
+        }
+        __syncthreads();
+        X = xs;
+        ldx = a.K;
     }
 
-    // 3. slice sums
-    float acc[RPW][kMaxRows];
+    // head: this block's best (value, index) per activation row, over all its rows
+    float bv = 0.f;
+    int bi = -1;
+    bool nan0 = false;
+
+    for (int blk = blockIdx.x; blk * RPB < n_iter_rows; blk += gridDim.x) {
+        const int row0 = (blk * GROUPS + grp) * RPW;
+        // 3. slice sums
+        float acc[RPW][kMaxRows];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r)
+        for (int r = 0; r < RPW; ++r)
 #pragma unroll
-        for (int m = 0; m < kMaxRows; ++m) acc[r][m] = 0.f;
+            for (int m = 0; m < kMaxRows; ++m) acc[r][m] = 0.f;
 #pragma unroll
-    for (int u = 0; u < CPL; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < c1) {
+        for (int u = 0; u < CPL; ++u) {
+            const int c = c0 + u * 32 + lane;
+            if (c < c1) {
+                if constexpr (WT == 0 && RPW == 1 && WS == 1 && CPL <= 8) {
+                    // every row's activation chunk first, then the sums
+                    float4 xv[kMaxRows];
 #pragma unroll
-            for (int m = 0; m < kMaxRows; ++m) {
-                if (m < a.M) {
-                    if constexpr (WT == 0) {
-                        const float4 xv = LN ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
-                                             : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
+                    for (int m = 0; m < kMaxRows; ++m)
+                        if (m < a.M)
+                            xv[m] = staged ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
+                                           : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
 #pragma unroll
-                        for (int r = 0; r < RPW; ++r) {
-                            float t = acc[r][m];
-                            t = fmaf(w[r][u].x, xv.x, t);
-                            t = fmaf(w[r][u].y, xv.y, t);
-                            t = fmaf(w[r][u].z, xv.z, t);
-                            t = fmaf(w[r][u].w, xv.w, t);
-                            acc[r][m] = t;
-                        }
-                    } else {
-#pragma unroll
-                        for (int q4 = 0; q4 < EPC / 4; ++q4) {
-                            const float* xp = X + (size_t)m * ldx + (size_t)c * EPC + 4 * q4;
-                            const float4 xv = LN ? *reinterpret_cast<const float4*>(xp)
-                                                 : __ldg(reinterpret_cast<const float4*>(xp));
+                    for (int m = 0; m < kMaxRows; ++m) {
+                        if (m < a.M) {
 #pragma unroll
                             for (int r = 0; r < RPW; ++r) {
                                 float t = acc[r][m];
-                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 0), xv.x, t);
-                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 1), xv.y, t);
-                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 2), xv.z, t);
-                                t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 3), xv.w, t);
+                                t = fmaf(w[r][u].x, xv[m].x, t);
+                                t = fmaf(w[r][u].y, xv[m].y, t);
+                                t = fmaf(w[r][u].z, xv[m].z, t);
+                                t = fmaf(w[r][u].w, xv[m].w, t);
                                 acc[r][m] = t;
                             }
                         }
                     }
+                } else {
+#pragma unroll
+                for (int m = 0; m < kMaxRows; ++m) {
+                    if (m < a.M) {
+                        {
+#pragma unroll
+                            for (int q4 = 0; q4 < EPC / 4; ++q4) {
+                                // (fp32: EPC / 4 == 1 and chunk_elem is the float4's lanes)
+                                const float* xp = X + (size_t)m * ldx + (size_t)c * EPC + 4 * q4;
+                                const float4 xv = staged ? *reinterpret_cast<const float4*>(xp)
+                                                         : __ldg(reinterpret_cast<const float4*>(xp));
+#pragma unroll
+                                for (int r = 0; r < RPW; ++r) {
+                                    float t = acc[r][m];
+                                    t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 0), xv.x, t);
+                                    t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 1), xv.y, t);
+                                    t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 2), xv.z, t);
+                                    t = fmaf(chunk_elem<WT>(w[r][u], 4 * q4 + 3), xv.w, t);
+                                    acc[r][m] = t;
+                                }
+                            }
+                        }
+                    }
+                }
                 }
             }
         }
-    }
-#pragma unroll
-    for (int r = 0; r < RPW; ++r)
-#pragma unroll
-        for (int m = 0; m < kMaxRows; ++m) {
-            if (m >= a.M) break;  // uniform across the block
-            float v = acc[r][m];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            acc[r][m] = v;
-        }
-    if (lane == 0) {
+        // the next group's weights go out while this group is finished
+        if ((blk + gridDim.x) * RPB < n_iter_rows) load(((blk + gridDim.x) * GROUPS + grp) * RPW);
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
-            for (int m = 0; m < kMaxRows; ++m) s_part[grp][ks][r][m] = acc[r][m];
-    }
-    __syncthreads();
-
-    // 4. epilogue: slice sums in slice order; thread t of a row group handles
-    //    (row r, activation row m) pairs
-    if constexpr (EPI != DEC_HEAD) {
-        const int t = threadIdx.x % (WS * 32);
-        if (warp % WS == 0 || WS == 1) {
-            for (int q = (WS == 1 ? lane : t); q < RPW * a.M; q += (WS == 1 ? 32 : WS * 32)) {
-                const int r = q / a.M, m = q % a.M;
-                const int j = row0 + r;
-                if (j >= a.N) continue;
-                float sum = s_part[grp][0][r][m];
+            for (int m = 0; m < kMaxRows; ++m) {
+                if (m >= a.M) break;  // uniform across the block
+                float v = acc[r][m];
 #pragma unroll
-                for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
-                if constexpr (WT == 2) sum = sum * __ldg(a.scale + j);
-                float* yp = a.y + (size_t)m * a.ldy + j;
-                float v;
-                if constexpr (EPI == DEC_BIAS || EPI == DEC_QKV_KV) v = apply_epi<EPI_BIAS>(sum, a.bias, j, yp);
-                else if constexpr (EPI == DEC_BIAS_GELU) v = apply_epi<EPI_BIAS_GELU>(sum, a.bias, j, yp);
-                else v = apply_epi<EPI_BIAS_RESID>(sum, a.bias, j, yp);
-                *yp = v;
-                if constexpr (EPI == DEC_QKV_KV) {
-                    const int E = a.kv.n_embd;
-                    if (j >= E) {
-                        const size_t row = a.kv.row(m, a.lens[m]);
-                        if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
-                        else a.kv.v[row * E + (j - 2 * E)] = v;
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                acc[r][m] = v;
+            }
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int m = 0; m < kMaxRows; ++m) s_part[grp][ks][r][m] = acc[r][m];
+        }
+        __syncthreads();
+
+        // 4. epilogue: slice sums in slice order; thread t of a row group
+        //    handles (row r, activation row m) pairs
+        if constexpr (EPI != DEC_HEAD) {
+            const int t = threadIdx.x % (WS * 32);
+            if (warp % WS == 0 || WS == 1) {
+                for (int q = (WS == 1 ? lane : t); q < RPW * a.M; q += (WS == 1 ? 32 : WS * 32)) {
+                    const int r = q / a.M, m = q % a.M;
+                    const int j = row0 + r;
+                    if (j >= a.N) continue;
+                    float sum = s_part[grp][0][r][m];
+#pragma unroll
+                    for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
+                    if constexpr (WT == 2) sum = sum * __ldg(a.scale + j);
+                    float* yp = a.y + (size_t)m * a.ldy + j;
+                    float v;
+                    if constexpr (EPI == DEC_BIAS || EPI == DEC_QKV_KV) v = apply_epi<EPI_BIAS>(sum, a.bias, j, yp);
+                    else if constexpr (EPI == DEC_BIAS_GELU) v = apply_epi<EPI_BIAS_GELU>(sum, a.bias, j, yp);
+                    else v = apply_epi<EPI_BIAS_RESID>(sum, a.bias, j, yp);
+                    *yp = v;
+                    if constexpr (EPI == DEC_QKV_KV) {
+                        const int E = a.kv.n_embd;
+                        if (j >= E) {
+                            const size_t row = a.kv.row(m, a.lens[m]);
+                            if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
+                            else a.kv.v[row * E + (j - 2 * E)] = v;
+                        }
                     }
                 }
             }
+        } else {
+            // logits (optional) and the running best per activation row; NaN
+            // at index 0 is reported as index -2 (the reference's scan never
+            // leaves index 0 then)
+            if ((int)threadIdx.x < a.M) {
+                const int m = threadIdx.x;
+                for (int g = 0; g < GROUPS; ++g)
+                    for (int r = 0; r < RPW; ++r) {
+                        const int j = (blk * GROUPS + g) * RPW + r;
+                        if (j >= a.N) continue;
+                        float v = s_part[g][0][r][m];
+                        for (int k = 1; k < WS; ++k) v += s_part[g][k][r][m];
+                        if constexpr (WT == 2) v = v * __ldg(a.scale + j);
+                        if (a.y) a.y[(size_t)m * a.ldy + j] = v;
+                        if (j == 0 && !(v == v)) nan0 = true;
+                        else if (v == v && beats(v, j, bv, bi)) { bv = v; bi = j; }
+                    }
+            }
         }
-    } else {
-        // logits (optional) and this block's best (value, index) per activation
-        // row; NaN at index 0 is reported as index -2 (the reference's scan never
-        // leaves index 0 then)
+        __syncthreads();   // s_part is rewritten by the next group
+    }
+    if constexpr (EPI == DEC_HEAD) {
         if ((int)threadIdx.x < a.M) {
-            const int m = threadIdx.x;
-            float bv = 0.f;
-            int bi = -1;
-            bool nan0 = false;
-            for (int g = 0; g < GROUPS; ++g)
-                for (int r = 0; r < RPW; ++r) {
-                    const int j = (blockIdx.x * GROUPS + g) * RPW + r;
-                    if (j >= a.N) continue;
-                    float v = s_part[g][0][r][m];
-                    for (int k = 1; k < WS; ++k) v += s_part[g][k][r][m];
-                    if constexpr (WT == 2) v = v * __ldg(a.scale + j);
-                    if (a.y) a.y[(size_t)m * a.ldy + j] = v;
-                    if (j == 0 && !(v == v)) nan0 = true;
-                    else if (v == v && beats(v, j, bv, bi)) { bv = v; bi = j; }
-                }
-            a.part_val[(size_t)blockIdx.x * a.M + m] = bv;
-            a.part_idx[(size_t)blockIdx.x * a.M + m] = nan0 ? -2 : bi;
+            a.part_val[(size_t)blockIdx.x * a.M + threadIdx.x] = bv;
+            a.part_idx[(size_t)blockIdx.x * a.M + threadIdx.x] = nan0 ? -2 : bi;
         }
     }
 }
 
+// Blocks of a launch: one per row group up to four per SM; the kernel walks
+// the remaining groups itself.
+int gemv_grid(int N, int rows_per_block) {
+    static int cap = 0;
+    if (!cap) {
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                      cudaSuccess) {
+            cudaGetLastError();
+            sms = 148;
+        }
+        cap = 4 * sms;
+    }
+    const int need = (N + rows_per_block - 1) / rows_per_block;
+    return need < cap ? need : cap;
+}
+
 template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
 cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
-    const size_t smem = LN ? (size_t)a.M * a.K * sizeof(float) : 0;
+    // the kernel stages the activation rows whenever it normalises them or
+    // they fit kStageFloats; that is exactly when it needs this much
+    const bool staged = LN || a.M * a.K <= kStageFloats;
+    const size_t smem = staged ? (size_t)a.M * a.K * sizeof(float) : 0;
     auto k = dec_gemv_kernel<EPI, LN, RPW, WS, CPL, WT>;
-    if (smem > 48 * 1024) {
+    if (smem > 32 * 1024) {   // with the static shared memory, beyond the default 48 KB
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     constexpr int rows_per_block = (kWarps / WS) * RPW;
-    const int grid = (a.N + rows_per_block - 1) / rows_per_block;
+    const int grid = gemv_grid(a.N, rows_per_block);
     cudaError_t e = launch_pdl(k, dim3(grid), dim3(kWarps * 32), smem, st, a);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
@@ -333,7 +404,7 @@ int chunk_elems(int wt) { return wt == 0 ? 4 : (wt == 1 ? 8 : 16); }
 // chunks (RPW 4, WS 1), else one row cut into 4 slices (RPW 1, WS 4).
 int dec_head_blocks(int V, int K, int wt) {
     const int rows = K / chunk_elems(wt) <= 256 ? kWarps * 4 : 1;
-    return (V + rows - 1) / rows;
+    return gemv_grid(V, rows);
 }
 
 // y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL. Weights

@@ -76,6 +76,10 @@ layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
     __shared__ __align__(16) float rs[kLnWarps][kLnMaxK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kLnWarps + warp;
+    // in a programmatic-dependent chain: let the next kernel start loading its
+    // weights, then wait for x
+    pdl_trigger();
+    pdl_wait();
     if (row >= rows) return;
     float* xr = rs[warp];
     const int E4 = E >> 2;
@@ -296,8 +300,9 @@ cudaError_t launch_layernorm(const float* x, const float* g, const float* b, flo
                              int E, float eps, cudaStream_t st, float* y_hi, float* y_lo) {
     if (E > kLnMaxK || (E & 3)) return cudaErrorInvalidValue;
     const int grid = (rows + kLnWarps - 1) / kLnWarps;
-    layernorm_kernel<<<grid, kLnWarps * 32, 0, st>>>(x, g, b, y, y_hi, y_lo, rows, E, eps);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(layernorm_kernel, dim3(grid), dim3(kLnWarps * 32), 0, st, x, g, b, y, y_hi, y_lo,
+                               rows, E, eps);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_kv_store_prefill(const float* qkv, int n_seq, int T, PagedKV kv, int first_seq,

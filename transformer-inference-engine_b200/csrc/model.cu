@@ -590,25 +590,29 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
     model_status rc;
     LAUNCH(launch_embed_decode(m->d_tokens, m->d_lens, B, m->wte, m->wpe, m->x, E, V, st));
     if (small) {
-        // fused, PDL-chained kernels: 5 per layer (k_decode.cu)
+        // PDL-chained kernels: 7 per layer (k_decode.cu, k_attn.cu, k_misc.cu)
         for (int l = 0; l < m->cfg.n_layer; ++l) {
             const Layer& w = m->layers[l];
             const QMat q0 = qmat(m, l, 0), q1 = qmat(m, l, 1), q2 = qmat(m, l, 2), q3 = qmat(m, l, 3);
             const PagedKV view = layer_view(cache, l);
-            LAUNCH(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, eps, w.qkv_w, w.qkv_b, m->qkv, 3 * E, B, 3 * E, E,
+            // LayerNorm once per row, then the matmul over the normalised rows
+            LAUNCH(launch_layernorm(m->x, w.ln1_w, w.ln1_b, m->xb, B, E, eps, st));
+            LAUNCH(launch_dec_gemv(m->xb, E, nullptr, nullptr, eps, w.qkv_w, w.qkv_b, m->qkv, 3 * E, B, 3 * E, E,
                                    EPI_QKV_KV, &view, m->d_lens, st, q0.wt, q0.q, q0.s));
             LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st,
                                       nullptr, nullptr, m->d_attn_cnt));
             if (stats) ++m->launches;  // the separate merge kernel
             LAUNCH(launch_dec_gemv(m->attn, E, nullptr, nullptr, eps, w.proj_w, w.proj_b, m->x, E, B, E, E,
                                    EPI_BIAS_RESID, nullptr, nullptr, st, q1.wt, q1.q, q1.s));
-            LAUNCH(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, eps, w.fc_w, w.fc_b, m->ff, 4 * E, B, 4 * E, E,
+            LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, B, E, eps, st));
+            LAUNCH(launch_dec_gemv(m->xb, E, nullptr, nullptr, eps, w.fc_w, w.fc_b, m->ff, 4 * E, B, 4 * E, E,
                                    EPI_BIAS_GELU, nullptr, nullptr, st, q2.wt, q2.q, q2.s));
             LAUNCH(launch_dec_gemv(m->ff, 4 * E, nullptr, nullptr, eps, w.mlp_w, w.mlp_b, m->x, E, B, E, 4 * E,
                                    EPI_BIAS_RESID, nullptr, nullptr, st, q3.wt, q3.q, q3.s));
         }
         const QMat qh = qmat(m, m->cfg.n_layer, 0);
-        LAUNCH(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
+        LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, B, E, eps, st));
+        LAUNCH(launch_dec_head(m->xb, E, nullptr, nullptr, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
                                m->d_am_idx, st, qh.wt, qh.q, qh.s));
         LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, qh.wt), B, m->d_next, st));
         if (advance)
@@ -1530,7 +1534,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
             case TIE_KERNEL_DECODE_QKV:
                 if (small) {
                     const QMat q = qmat(m, 0, 0);
-                    CU(launch_dec_gemv(m->x, E, w.ln1_w, w.ln1_b, m->cfg.layer_norm_epsilon, w.qkv_w, w.qkv_b, m->qkv,
+                    CU(launch_dec_gemv(m->xb, E, nullptr, nullptr, 0.f, w.qkv_w, w.qkv_b, m->qkv,
                                        3 * E, B, 3 * E, E, EPI_QKV_KV, &view, m->d_lens, st, q.wt, q.q, q.s));
                     return MODEL_OK;
                 }
@@ -1539,7 +1543,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
             case TIE_KERNEL_DECODE_FC:
                 if (small) {
                     const QMat q = qmat(m, 0, 2);
-                    CU(launch_dec_gemv(m->x, E, w.ln2_w, w.ln2_b, m->cfg.layer_norm_epsilon, w.fc_w, w.fc_b, m->ff,
+                    CU(launch_dec_gemv(m->xb, E, nullptr, nullptr, 0.f, w.fc_w, w.fc_b, m->ff,
                                        4 * E, B, 4 * E, E, EPI_BIAS_GELU, nullptr, nullptr, st, q.wt, q.q, q.s));
                     return MODEL_OK;
                 }
@@ -1557,7 +1561,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
             case TIE_KERNEL_DECODE_HEAD:
                 if (small) {
                     const QMat q = qmat(m, m->cfg.n_layer, 0);
-                    CU(launch_dec_head(m->x, E, m->lnf_w, m->lnf_b, m->cfg.layer_norm_epsilon, m->wte, m->logits, V,
+                    CU(launch_dec_head(m->xb, E, nullptr, nullptr, 0.f, m->wte, m->logits, V,
                                        B, V, E, m->d_am_val, m->d_am_idx, st, q.wt, q.q, q.s));
                     CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, q.wt), B, m->d_next,
                                               st));
