@@ -199,11 +199,12 @@ cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float
 // (model.c:826-850).
 int attn_decode_max_splits(int capacity);
 // With `counters` (B * H ints, zero on first use; the kernel leaves them zero)
-// and no statistics, one fused kernel; else split + merge kernels.
+// and no statistics, one fused kernel; else split + merge kernels. `err` is
+// set when a bounded wait of the large-batch kernel expires.
 cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv,
                                int max_splits, float* part, float* out, AttnStats* stats,
                                cudaStream_t st, float* out_hi = nullptr, float* out_lo = nullptr,
-                               int* counters = nullptr);
+                               int* counters = nullptr, int* err = nullptr);
 
 // Small-batch (<= 16 rows) decode matmuls with optional LayerNorm prologue
 // (ln_g non-NULL) and PDL chaining (k_decode.cu). Weights fp32 (W), or with wt

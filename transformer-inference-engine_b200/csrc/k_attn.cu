@@ -15,6 +15,8 @@
 // With statistics enabled (reference model_collect_attn_stats) a second pass
 // recomputes each row's normalised probabilities from the same scores and
 // records the min and max of their double-precision sums.
+#include <algorithm>
+
 #include "common.cuh"
 #include "tc_gemm.h"
 
@@ -473,6 +475,275 @@ attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restric
     if (tid == 0) counters[b * H + h] = 0;
 }
 
+constexpr int PG = 16;   // positions per page and per chunk
+static_assert(PG == kPageRows, "a chunk is one page");
+
+// Large batches, persistent, one warp per unit: a unit is up to kUnitChunks
+// consecutive 16-position chunks of one (sequence, head). Units are numbered
+// (sequence, split, head), head fastest; each CTA takes a contiguous range of
+// them and its warps take the range's units in turn, so a CTA reads a few
+// neighbouring pages at a time.
+//
+// A warp keeps its chunk's keys and values in registers -- lane 2 pi + half
+// the half of key pi it scores (8 x 16 bytes), lane l value dims 2l, 2l + 1
+// of all 16 positions -- and software-pipelines across chunks in those same
+// registers: as soon as a chunk's scores are formed its key registers receive
+// the next chunk's keys, and once its weighted values are summed the value
+// registers receive the next chunk's values. Page-table entries are looked up
+// one chunk ahead and the next unit's query is fetched while the current unit
+// runs, so loads stay in flight through the whole loop. Decode attention reads
+// every K and V element exactly once; nothing is staged in shared memory.
+//
+// Each chunk is reduced with the arithmetic of attn_decode_fused_kernel<16>
+// -- lane 2 pi + half scores position pi over its half of the dims, then the
+// chunk max, the probabilities summed in position order, and the weighted
+// values as eight position groups added in group order -- and merged with its
+// formula, so results are bit-identical to the small-batch path. A unit's chunk partials are counted in with one acquire-release
+// atomic per (sequence, head); the warp completing the count merges.
+constexpr int kUnitChunks = 4;
+constexpr int kWarpThreads = 256;
+constexpr int kWarpsPerCta = kWarpThreads / 32;
+constexpr int kWarpMaxSeqs = 8192;
+
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ float4 ld_stream4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float2 ld_stream2(const float* p) { return __ldcs(reinterpret_cast<const float2*>(p)); }
+
+// the sequence holding unit u, searching s_start[0..B] (s_start[B] = total)
+__device__ __forceinline__ int unit_seq(const int* s_start, int B, int u) {
+    int lo = 0, hi = B;   // s_start[lo] <= u < s_start[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_start[mid] <= u) lo = mid;
+        else hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ int units_of(int ctx, int H) {
+    return H * ((ctx + PG * kUnitChunks - 1) / (PG * kUnitChunks));
+}
+
+// a warp's position in its chunk sequence: unit u (valid while u < end),
+// sequence b, head h, chunk c of the unit's chunks [.., c1), context ctx
+struct ChunkCursor {
+    int u, b, h, c, c1, ctx;
+    __device__ __forceinline__ void unit(int uu, const int* s_start, const int* s_ctx, int B, int H, int end) {
+        u = uu;
+        if (u >= end) return;
+        b = unit_seq(s_start, B, u);
+        const int r = u - s_start[b], split = r / H;
+        h = r - split * H;
+        ctx = s_ctx[b];
+        c = split * kUnitChunks;
+        c1 = min((ctx + PG - 1) / PG, c + kUnitChunks);
+    }
+    // the next chunk; returns true when it starts a new unit
+    __device__ __forceinline__ bool next(const int* s_start, const int* s_ctx, int B, int H, int end) {
+        if (++c < c1) return false;
+        unit(u + kWarpsPerCta, s_start, s_ctx, B, H, end);
+        return true;
+    }
+    __device__ __forceinline__ int rows() const { return min(PG, ctx - c * PG); }
+};
+
+__global__ void __launch_bounds__(kWarpThreads, 2)
+attn_decode_warp_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int B, int H, PagedKV kv,
+                        int max_splits, float scale, float* __restrict__ part, int* __restrict__ counters,
+                        float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo) {
+    extern __shared__ int s_seq[];
+    int* s_start = s_seq;           // [B + 1] unit offsets
+    int* s_ctx = s_seq + B + 1;     // [B] contexts
+    __shared__ float4 s_q[kWarpsPerCta][D / 4];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    pdl_wait();
+    {
+        // contexts and unit offsets of every sequence: a block-wide exclusive scan
+        const int seg = (B + kWarpThreads - 1) / kWarpThreads, j0 = min(B, tid * seg), j1 = min(B, j0 + seg);
+        int local = 0;
+        for (int j = j0; j < j1; ++j) {
+            s_ctx[j] = lens[j] + 1;
+            local += units_of(s_ctx[j], H);
+        }
+        int v = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += y;
+        }
+        __shared__ int s_wsum[kWarpsPerCta];
+        if (lane == 31) s_wsum[warp] = v;
+        __syncthreads();
+        int run = v - local;
+        for (int w = 0; w < warp; ++w) run += s_wsum[w];
+        for (int j = j0; j < j1; ++j) {
+            s_start[j] = run;
+            run += units_of(s_ctx[j], H);
+        }
+        if (j0 < j1 && j1 == B) s_start[B] = run;
+        __syncthreads();
+    }
+    const int total = s_start[B];
+    const int u_lo = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int end = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    if (u_lo + warp >= end) return;
+    const int E = kv.n_embd;
+    const int pi = lane >> 1, half = lane & 1;
+    const float4* qs = s_q[warp];
+    auto q_ptr = [&](const ChunkCursor& q) { return qkv + (size_t)q.b * 3 * E + q.h * D; };
+
+    ChunkCursor cc, nx;
+    cc.unit(u_lo + warp, s_start, s_ctx, B, H, end);
+    if (lane < D / 4) s_q[warp][lane] = *reinterpret_cast<const float4*>(q_ptr(cc) + 4 * lane);
+    float4 k4[8];
+    float2 v2[PG];
+    {
+        const size_t row0 = kv.row(cc.b, cc.c * PG);
+        const int n = cc.rows();
+        const float* kp = kv.k + (row0 + pi) * E + cc.h * D;
+        if (pi < n) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) k4[j] = ld_stream4(kp + 4 * (2 * j + half));
+        }
+#pragma unroll
+        for (int i = 0; i < PG; ++i)
+            if (i < n) v2[i] = ld_stream2(kv.v + (row0 + i) * E + cc.h * D + 2 * lane);
+    }
+    nx = cc;
+    bool nx_new = nx.next(s_start, s_ctx, B, H, end);
+    float4 qn = make_float4(0.f, 0.f, 0.f, 0.f);   // lanes < 16: the next unit's query
+    size_t nx_row = 0;
+    if (nx.u < end) {
+        nx_row = kv.row(nx.b, nx.c * PG);
+        if (nx_new && lane < D / 4) qn = *reinterpret_cast<const float4*>(q_ptr(nx) + 4 * lane);
+    }
+    __syncwarp();
+    int run_n = 0;
+    while (true) {
+        const int n = cc.rows();
+        const bool more = nx.u < end;
+        const int nn = more ? nx.rows() : 0;
+        // scores of this chunk; then the key registers take the next chunk's keys
+        float a = 0.f;
+        if (pi < n) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 q4 = qs[2 * j + half];
+                a = fmaf(q4.x, k4[j].x, a);
+                a = fmaf(q4.y, k4[j].y, a);
+                a = fmaf(q4.z, k4[j].z, a);
+                a = fmaf(q4.w, k4[j].w, a);
+            }
+        }
+        if (pi < nn) {
+            const float* kp = kv.k + (nx_row + pi) * E + nx.h * D;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) k4[j] = ld_stream4(kp + 4 * (2 * j + half));
+        }
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        const float sc = pi < n ? a * scale : -INFINITY;
+        float mx = sc;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e = pi < n ? expf(sc - mx) : 0.f;
+        float l = 0.f;
+#pragma unroll
+        for (int i = 0; i < PG; ++i) {
+            const float ei = __shfl_sync(0xffffffffu, e, 2 * i);
+            if (i < n) l += ei;
+        }
+        // weighted values; then the value registers take the next chunk's values
+        float ox = 0.f, oy = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const float e0 = __shfl_sync(0xffffffffu, e, 2 * g);
+            const float e1 = __shfl_sync(0xffffffffu, e, 2 * (g + 8));
+            float ax = 0.f, ay = 0.f;
+            if (g < n) {
+                ax = fmaf(e0, v2[g].x, ax);
+                ay = fmaf(e0, v2[g].y, ay);
+            }
+            if (g + 8 < n) {
+                ax = fmaf(e1, v2[g + 8].x, ax);
+                ay = fmaf(e1, v2[g + 8].y, ay);
+            }
+            if (g == 0) { ox = ax; oy = ay; }
+            else { ox += ax; oy += ay; }
+        }
+#pragma unroll
+        for (int i = 0; i < PG; ++i)
+            if (i < nn) v2[i] = ld_stream2(kv.v + (nx_row + i) * E + nx.h * D + 2 * lane);
+        float* pbase = part + (size_t)(cc.b * H + cc.h) * max_splits * PART;
+        float* pp = pbase + (size_t)cc.c * PART;
+        *reinterpret_cast<float2*>(pp + 2 + 2 * lane) = make_float2(ox, oy);
+        if (lane == 0) *reinterpret_cast<float2*>(pp) = make_float2(mx, l);
+        ++run_n;
+
+        if (cc.c + 1 == cc.c1) {
+            // the unit is done: count its chunks in; the warp completing the count merges
+            const int ns = (cc.ctx + PG - 1) / PG;
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atom_add_acq_rel(&counters[cc.b * H + cc.h], run_n) + run_n == ns;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            run_n = 0;
+            if (last) {
+                __syncwarp();   // lane 0 acquired the other warps' partials for the whole warp
+                float m = -INFINITY;
+                for (int k = lane; k < ns; k += 32) m = fmaxf(m, __ldcg(pbase + (size_t)k * PART));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                float lt = 0.f, o0 = 0.f, o1 = 0.f;
+                for (int k0 = 0; k0 < ns; k0 += 4) {
+                    float2 ml[4], ov[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (k0 + k < ns) {
+                            ml[k] = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + k) * PART));
+                            ov[k] = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + k) * PART + 2 + 2 * lane));
+                        }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (k0 + k < ns) {
+                            const float cf = expf(ml[k].x - m);
+                            lt = fmaf(ml[k].y, cf, lt);
+                            o0 = fmaf(ov[k].x, cf, o0);
+                            o1 = fmaf(ov[k].y, cf, o1);
+                        }
+                }
+                const float y0 = o0 / lt, y1 = o1 / lt;
+                const size_t oi = (size_t)cc.b * H * D + cc.h * D + 2 * lane;
+                if (out) *reinterpret_cast<float2*>(out + oi) = make_float2(y0, y1);
+                if (out_hi) {
+                    const float h0 = tf32_hi(y0), h1 = tf32_hi(y1);
+                    *reinterpret_cast<float2*>(out_hi + oi) = make_float2(h0, h1);
+                    *reinterpret_cast<float2*>(out_lo + oi) = make_float2(__fsub_rn(y0, h0), __fsub_rn(y1, h1));
+                }
+                if (lane == 0) counters[cc.b * H + cc.h] = 0;
+            }
+        }
+        if (!more) break;
+        // advance: the next chunk becomes current
+        if (nx_new) {
+            __syncwarp();
+            if (lane < D / 4) s_q[warp][lane] = qn;
+            __syncwarp();
+        }
+        cc = nx;
+        nx_new = nx.next(s_start, s_ctx, B, H, end);
+        if (nx.u < end) {
+            nx_row = kv.row(nx.b, nx.c * PG);
+            if (nx_new && lane < D / 4) qn = *reinterpret_cast<const float4*>(q_ptr(nx) + 4 * lane);
+        }
+    }
+}
+
 }  // namespace
 
 // Partial-buffer sizing: the finest chunking any launch uses (16 positions).
@@ -498,7 +769,7 @@ cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float
 // B * H * max_splits * CH floats after the partials for the probabilities.
 cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv,
                                int max_splits, float* part, float* out, AttnStats* stats,
-                               cudaStream_t st, float* out_hi, float* out_lo, int* counters) {
+                               cudaStream_t st, float* out_hi, float* out_lo, int* counters, int* err) {
     if (B <= 0) return cudaSuccess;
     const float scale = (float)(1.0 / sqrt((double)D));
     if (stats || !counters) max_splits = (max_splits * 16 + CH - 1) / CH;  // 64-position chunks
@@ -509,11 +780,30 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
         attn_decode_split_kernel<true><<<g1, 128, 0, st>>>(qkv, lens, H, kv, max_splits, scale, part, e, e_ld);
         attn_decode_combine_kernel<true><<<g2, D, 0, st>>>(lens, H, max_splits, part, out, out_hi, out_lo, e, e_ld, stats);
     } else if (counters) {
-        // 16-position chunks while the batch is small (more blocks in flight),
-        // 64-position chunks otherwise; `max_splits` is the sizing bound
+        // 16-position chunks, a block each, while the batch is small; the
+        // persistent warp-per-unit kernel for larger batches; 64-position
+        // chunks beyond the sequences it indexes; `max_splits` is the sizing bound
         const int capacity = max_splits * 16;
         const bool fine = B <= 16;
         const int splits = fine ? max_splits : (capacity + CH - 1) / CH;
+        if (!fine && B <= kWarpMaxSeqs && kv.n_embd == H * D) {
+            // persistent, a warp per unit, loads pipelined in registers
+            int dev = 0, sms = 0;
+            cudaGetDevice(&dev);
+            cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+            const size_t smem = (size_t)(2 * B + 1) * sizeof(int);
+            if (smem > 48 * 1024) {
+                e = cudaFuncSetAttribute(attn_decode_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+                if (e != cudaSuccess) return e;
+            }
+            const long long units = (long long)B * H * ((max_splits + kUnitChunks - 1) / kUnitChunks);
+            const int grid = (int)std::min<long long>((units + kWarpsPerCta - 1) / kWarpsPerCta, 2LL * sms);
+            e = launch_pdl(attn_decode_warp_kernel, dim3(grid), dim3(kWarpThreads), smem, st, qkv, lens, B, H, kv,
+                           max_splits, scale, part, counters, out, out_hi, out_lo);
+            return e != cudaSuccess ? e : cudaGetLastError();
+        }
         cudaError_t e = fine ? launch_pdl(attn_decode_fused_kernel<16>, dim3(splits, H, B), dim3(128), 0, st, qkv,
                                           lens, H, kv, splits, scale, part, counters, out, out_hi, out_lo)
                              : launch_pdl(attn_decode_fused_kernel<CH>, dim3(splits, H, B), dim3(128), 0, st, qkv,

@@ -18,7 +18,7 @@
 //                    an mbarrier per slot. Nothing it copies is computed in the
 //                    step, so it runs ahead of the consumers by the whole ring,
 //                    across stage boundaries.
-//   warps 1..8       the consumers. Per stage they wait for the stage's inputs
+//   warps 1..7       the consumers. Per stage they wait for the stage's inputs
 //                    (a counter reaching its target), stage the activation rows
 //                    in shared memory (LayerNorm applied there where the stage
 //                    starts with one), and reduce each weight row of the slots
@@ -44,6 +44,7 @@
 // Waits are bounded (1 s on the global timer); on expiry the kernel sets *err,
 // lets its copies in flight land and returns.
 #include "common.cuh"
+#include "mbar.cuh"
 
 #include <cstddef>
 
@@ -61,98 +62,9 @@ constexpr int CHT = 16;                         // positions per attention chunk
 constexpr int kUnitChunks = 2 * kCons;          // chunks per attention unit (2 per warp)
 constexpr int kMaxPages = 64;
 constexpr int kMaxResid = 32;                   // residual columns a CTA keeps
-constexpr int kRegChunks = 6;                   // activation chunks per lane kept in registers (batch 1)                   // page-table entries per sequence kept in smem
-constexpr unsigned long long kWaitNs = 1000000000ull;
+constexpr int kRegChunks = 6;                   // activation chunks per lane kept in registers (batch 1)
 
-// ------------------------------------------------------------ primitives --
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ unsigned long long gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// bounded wait for the phase of `parity` to complete
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-    if (mbar_test(b, parity)) return true;
-    const unsigned long long t0 = gtime();
-    while (!mbar_try(b, parity))
-        if (gtime() - t0 > kWaitNs) return false;
-    return true;
-}
-// global -> shared bulk copy completing on `bar`; weights are read once per
-// step, so they are marked first to leave L2 (the KV cache and activations stay)
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                          uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-__device__ __forceinline__ uint64_t evict_last_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-// global -> L2 bulk prefetch
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes, uint64_t policy) {
-    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes),
-                 "l"(policy)
-                 : "memory");
-}
-__device__ __forceinline__ void bar_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 __device__ __forceinline__ void cons_sync() { bar_sync(1, kCons * 32); }
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-// count one completion; the writes this thread has seen (the CTA's, through
-// the barrier before it) become visible to whoever acquires the count
-__device__ __forceinline__ void signal(unsigned* p) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
-}
 // activations written earlier in this kernel by other CTAs: read at L2, never
 // from a possibly stale L1 line
 __device__ __forceinline__ float4 ld_cg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }

@@ -600,7 +600,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
             LAUNCH(launch_dec_gemv(m->xb, E, nullptr, nullptr, eps, w.qkv_w, w.qkv_b, m->qkv, 3 * E, B, 3 * E, E,
                                    EPI_QKV_KV, &view, m->d_lens, st, q0.wt, q0.q, q0.s));
             LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st,
-                                      nullptr, nullptr, m->d_attn_cnt));
+                                      nullptr, nullptr, m->d_attn_cnt, m->d_err));
             if (stats) ++m->launches;  // the separate merge kernel
             LAUNCH(launch_dec_gemv(m->attn, E, nullptr, nullptr, eps, w.proj_w, w.proj_b, m->x, E, B, E, E,
                                    EPI_BIAS_RESID, nullptr, nullptr, st, q1.wt, q1.q, q1.s));
@@ -628,7 +628,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
             return rc;
         LAUNCH(launch_kv_store_decode(m->qkv, m->d_lens, B, view, st));
         LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, nullptr, stats, st,
-                                  m->attn_hi, m->attn_lo, m->d_attn_cnt));
+                                  m->attn_hi, m->attn_lo, m->d_attn_cnt, m->d_err));
         if (stats) ++m->launches;  // the separate merge kernel
         if ((rc = matmul(m, true, B, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
                          EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
@@ -771,7 +771,6 @@ model_status finish(model* m) {
             cudaMemset(m->d_err, 0, sizeof(int));
             // a step that gave up leaves its counters wherever it stopped
             if (m->d_sync) cudaMemset(m->d_sync, 0, step_sync_words(m->cfg.n_layer) * sizeof(unsigned));
-            if (m->d_attn_cnt) cudaMemset(m->d_attn_cnt, 0, m->cnt_cap * sizeof(int));
             if (m->d_attn_cnt) cudaMemset(m->d_attn_cnt, 0, m->cnt_cap * sizeof(int));
             return MODEL_ERR_DEVICE;
         }
@@ -1529,7 +1528,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
             case TIE_KERNEL_DECODE_ATTENTION:
                 CU(launch_attn_decode(m->qkv, m->d_lens, B, H, view, splits, m->d_part, small ? m->attn : nullptr,
                                       nullptr, st, small ? nullptr : m->attn_hi, small ? nullptr : m->attn_lo,
-                                      m->d_attn_cnt));
+                                      m->d_attn_cnt, m->d_err));
                 return MODEL_OK;
             case TIE_KERNEL_DECODE_QKV:
                 if (small) {
