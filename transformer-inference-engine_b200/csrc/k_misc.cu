@@ -65,33 +65,62 @@ __global__ void embed_decode_kernel(const int32_t* __restrict__ tokens,
 // common.cuh). One warp per row; the row is first staged in shared memory
 // with all its 16-byte loads in flight, so the statistics do not wait on one
 // load at a time.
-constexpr int kLnWarps = 4;
-constexpr int kLnMaxK = 2048;
+// One block of kLnGroups warps per row: warp w is canonical group w, so the
+// eight group butterflies run at once; the group sums are then added in group
+// order by every thread (common.cuh's order exactly).
+constexpr int kLnThreads = 32 * kLnGroups;   // 256 virtual lanes
+constexpr int kLnMaxPer = 8;                 // terms per thread: E <= 2048
 
-__global__ void __launch_bounds__(kLnWarps * 32)
+__global__ void __launch_bounds__(kLnThreads)
 layernorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
                  const float* __restrict__ bvec, float* __restrict__ y,
                  float* __restrict__ y_hi, float* __restrict__ y_lo,
                  int rows, int E, float eps) {
-    __shared__ __align__(16) float rs[kLnWarps][kLnMaxK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kLnWarps + warp;
+    __shared__ double s_grp[2][kLnGroups];
+    const int v = threadIdx.x, w = v >> 5;
+    const int row = blockIdx.x;
     // in a programmatic-dependent chain: let the next kernel start loading its
     // weights, then wait for x
     pdl_trigger();
     pdl_wait();
     if (row >= rows) return;
-    float* xr = rs[warp];
-    const int E4 = E >> 2;
-    const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * E);
-    for (int c = lane; c < E4; c += 32) reinterpret_cast<float4*>(xr)[c] = src[c];
-    __syncwarp();
-    double mean;
-    float inv;
-    ln_stats_warp(xr, E, eps, lane, mean, inv);
+    const float* xr = x + (size_t)row * E;
+    float xv[kLnMaxPer];
+#pragma unroll
+    for (int j = 0; j < kLnMaxPer; ++j) xv[j] = v + kLnThreads * j < E ? xr[v + kLnThreads * j] : 0.f;
+    // mean: virtual lane v adds its terms v, v + 256, ... in order
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPer; ++j)
+        if (v + kLnThreads * j < E) s = __dadd_rn(s, (double)xv[j]);
+    s = ln_warp_sum_d(s);
+    if ((v & 31) == 0) s_grp[0][w] = s;
+    __syncthreads();
+    double S = s_grp[0][0];
+#pragma unroll
+    for (int k = 1; k < kLnGroups; ++k) S = __dadd_rn(S, s_grp[0][k]);
+    const double mean = S / (double)E;
+    // biased variance, same order
+    double q = 0.0;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPer; ++j)
+        if (v + kLnThreads * j < E) {
+            const double d = __dadd_rn((double)xv[j], -mean);
+            q = __dadd_rn(q, __dmul_rn(d, d));
+        }
+    q = ln_warp_sum_d(q);
+    if ((v & 31) == 0) s_grp[1][w] = q;
+    __syncthreads();
+    double V = s_grp[1][0];
+#pragma unroll
+    for (int k = 1; k < kLnGroups; ++k) V = __dadd_rn(V, s_grp[1][k]);
+    const float inv = (float)(1.0 / sqrt(__dadd_rn(V / (double)E, (double)eps)));
     const size_t off = (size_t)row * E;
-    for (int i = lane; i < E; i += 32) {
-        const float val = ln_apply(xr[i], mean, inv, g[i], bvec[i]);
+#pragma unroll
+    for (int j = 0; j < kLnMaxPer; ++j) {
+        const int i = v + kLnThreads * j;
+        if (i >= E) break;
+        const float val = ln_apply(xv[j], mean, inv, g[i], bvec[i]);
         if (y) y[off + i] = val;
         if (y_hi) {
             const float h = tf32_hi(val);
@@ -298,9 +327,9 @@ cudaError_t launch_embed_decode(const int32_t* tokens, const int32_t* lens, int 
 
 cudaError_t launch_layernorm(const float* x, const float* g, const float* b, float* y, int rows,
                              int E, float eps, cudaStream_t st, float* y_hi, float* y_lo) {
-    if (E > kLnMaxK || (E & 3)) return cudaErrorInvalidValue;
-    const int grid = (rows + kLnWarps - 1) / kLnWarps;
-    cudaError_t e = launch_pdl(layernorm_kernel, dim3(grid), dim3(kLnWarps * 32), 0, st, x, g, b, y, y_hi, y_lo,
+    if (E > kLnThreads * kLnMaxPer) return cudaErrorInvalidValue;
+    if (rows <= 0) return cudaSuccess;
+    cudaError_t e = launch_pdl(layernorm_kernel, dim3(rows), dim3(kLnThreads), 0, st, x, g, b, y, y_hi, y_lo,
                                rows, E, eps);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

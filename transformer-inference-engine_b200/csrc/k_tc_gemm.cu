@@ -10,18 +10,20 @@
 // fp32-level, where a plain tf32 product would be near 2^-11. (The split is the
 // published "3xTF32" scheme.)
 //
-// Structure (one 128 x BN output tile per CTA, 192 threads):
-//   warp 0      TMA producer: 4 tiles per 32-wide k-block (A hi/lo, B hi/lo),
-//               128-byte swizzled, into a STAGES-deep shared-memory ring
+// Structure (one 128 x BN output tile at a time per CTA, 192 threads):
+//   warp 0      TMA producer: 4 tiles per 16-wide k-block (A hi/lo, B hi/lo:
+//               64-byte rows, 64-byte swizzled) into a shared-memory ring
 //   warp 1      allocates the TMEM accumulator and issues the MMAs (one thread),
 //               committing each stage back to the producer
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32 TMEM
 //               lanes), apply bias / GELU / residual, store fp32 and/or the
 //               hi/lo split the next matmul consumes
-// A grid z-dimension splits K: each split writes raw partial sums that
-// tc_splitk_reduce adds in split order (deterministic) and finishes with the
-// epilogue. The split count depends only on N and K, never on M, so a row's
-// result does not depend on how many rows are in the batch.
+// tc_gemm_kernel (prefill) is persistent over the output tiles with a double-
+// buffered accumulator. tc_gemm_split_kernel (decode shapes) splits K across
+// the CTAs of a thread-block cluster and sums the splits through distributed
+// shared memory in split order. The split count depends only on N and K,
+// never on M, so a row's result does not depend on how many rows are in the
+// batch.
 //
 // Every wait on an mbarrier is bounded; on expiry the kernel records an error
 // flag, still drains its own TMA copies and MMAs, frees its TMEM and returns.
@@ -67,19 +69,6 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
-}
-
-// Bounded wait: false (and the error flag set) if the phase has not completed
-// within kWaitLimitNs of wall time.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
-    atomicExch(err, 1);
-    return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
@@ -305,19 +294,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                 if (!ok || row >= p.M) continue;
                 const int col0 = n0 + c * 32;
                 const bool full_chunk = col0 + 32 <= p.N;
-                if constexpr (OUT == TC_OUT_PARTIAL) {
-                    float* dst = p.partial + ((size_t)z * p.M + row) * p.N + col0;
-                    if (full_chunk && (p.N & 3) == 0) {
-#pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4)
-                            reinterpret_cast<float4*>(dst)[i4] =
-                                make_float4(__uint_as_float(v[4 * i4]), __uint_as_float(v[4 * i4 + 1]),
-                                            __uint_as_float(v[4 * i4 + 2]), __uint_as_float(v[4 * i4 + 3]));
-                    } else {
-                        for (int k = 0; k < 32; ++k)
-                            if (col0 + k < p.N) dst[k] = __uint_as_float(v[k]);
-                    }
-                } else {
+                {
                     const size_t o = (size_t)row * p.ldc + col0;
                     float y[32];
 #pragma unroll
@@ -368,23 +345,239 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     }
 }
 
-// Sum of the split partials in split order, then the epilogue.
+// ---------------------------------------------------------------------------
+// Decode-sized matmuls: split-K across a thread-block cluster.
+//
+// Grid (splits, N tiles, M tiles), cluster (splits, 1, 1): the CTAs of a
+// cluster compute the K splits of one 128 x 128 output tile. Each accumulates
+// its split in TMEM (the same TMA ring and three MMAs per k-step as
+// tc_gemm_kernel, three stages so that two CTAs fit on an SM), then stages the
+// raw partial in its own shared memory over the drained ring. After a cluster
+// barrier, CTA z sums rows [z R, (z + 1) R) of the tile, R = 128 / splits,
+// reading every CTA's partial through distributed shared memory in split
+// order (the order of tc_splitk_reduce, so the result does not depend on
+// which kernel reduced it), applies the epilogue and stores. No partial goes
+// through global memory and there is no second kernel.
+//
+// Launched with programmatic dependent launch: the weight (B) tiles of the
+// first stages are requested before griddepcontrol.wait, the activation (A)
+// tiles and every read of a previous kernel's output after it.
+constexpr int kSplitStages = 3;
+constexpr int kRedLd = 128 + 4;   // staging row stride in floats: conflict-free float4 stores down a column
+static_assert((size_t)kSplitStages * (2u * BM * 64 + 2u * 128 * 64) >= (size_t)BM * kRedLd * sizeof(float),
+              "the partial overlays the drained ring");
+
+constexpr size_t split_smem_bytes() {
+    return 1024 + (size_t)kSplitStages * (2u * BM * 64 + 2u * 128 * 64) + 256;
+}
+
+__device__ __forceinline__ uint32_t mapa_cluster(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 template <int EPI, int OUT>
-__global__ void tc_splitk_reduce(TcArgs p, int splits) {
-    const long long n = (long long)p.M * p.N;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int row = (int)(i / p.N), col = (int)(i % p.N);
-        float acc = p.partial[i];
-        for (int z = 1; z < splits; ++z) acc = __fadd_rn(acc, p.partial[(size_t)z * n + i]);
-        const size_t o = (size_t)row * p.ldc + col;
-        const float y = apply_epi<EPI>(acc, p.bias, col, p.C + o);
-        if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o] = y;
-        if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
-            const float hi = tf32_hi(y);
-            p.C_hi[o] = hi;
-            p.C_lo[o] = __fsub_rn(y, hi);
+__global__ void __launch_bounds__(THREADS, 2)
+tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                     const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                     TcArgs p) {
+    constexpr int BN = 128, S = kSplitStages;
+    constexpr uint32_t kStage = stage_bytes<BN>();
+    constexpr uint32_t kTileA = BM * 64, kTileB = BN * 64;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage);
+    uint64_t* full = bars;          // [S]  TMA -> MMA
+    uint64_t* empty = bars + S;     // [S]  MMA -> TMA
+    uint64_t* tfull = bars + 2 * S; // [1]  MMA -> epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(smem);   // [BM][kRedLd] once the ring has drained
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int z = blockIdx.x, splits = gridDim.x;
+    const int n0 = blockIdx.y * BN, m0 = blockIdx.z * BM;
+    const int kb0 = z * p.kb_per_split;
+    const int nkb = min(p.kb_per_split, p.K / BK - kb0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
         }
+        mbar_init(smem_u32(&tfull[0]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+    grid_dep_trigger();
+
+    auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (mbar_try_wait(bar, parity)) return true;
+            if ((i & 255u) == 0) {
+                if (*abort_flag) return false;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
+        }
+        *abort_flag = 1;
+        atomicExch(p.err, 1);
+        return false;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            const int pre = min(S, nkb);
+            // weights first: they do not depend on the previous kernel
+            for (int kb = 0; kb < pre; ++kb) {
+                const uint32_t base = smem_u32(smem + kb * kStage);
+                const uint32_t fb = smem_u32(&full[kb]);
+                mbar_expect_tx(fb, kStage);
+                const int kx = (kb0 + kb) * BK;
+                tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
+                tma_load_2d(base + 2 * kTileA + kTileB, &tb_lo, fb, kx, n0);
+            }
+            grid_dep_wait();
+            for (int kb = 0; kb < pre; ++kb) {
+                const uint32_t base = smem_u32(smem + kb * kStage);
+                const uint32_t fb = smem_u32(&full[kb]);
+                const int kx = (kb0 + kb) * BK;
+                tma_load_2d(base, &ta_hi, fb, kx, m0);
+                tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
+            }
+            int kb = pre;
+            for (; kb < nkb; ++kb) {
+                const int s = kb % S;
+                if (!wait(smem_u32(&empty[s]), ((kb / S) & 1u) ^ 1u)) break;
+                const uint32_t base = smem_u32(smem + s * kStage);
+                const uint32_t fb = smem_u32(&full[s]);
+                mbar_expect_tx(fb, kStage);
+                const int kx = (kb0 + kb) * BK;
+                tma_load_2d(base, &ta_hi, fb, kx, m0);
+                tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
+                tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
+                tma_load_2d(base + 2 * kTileA + kTileB, &tb_lo, fb, kx, n0);
+            }
+            // every copy this thread started has landed before the ring is reused
+            for (int j = kb > S ? kb - S : 0; j < kb; ++j) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(&full[j % S]), (j / S) & 1u))
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) { atomicExch(p.err, 1); break; }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32<BN>();
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                if (!wait(smem_u32(&full[s]), (kb / S) & 1u)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t base = smem_u32(smem + s * kStage);
+#pragma unroll
+                for (int j = 0; j < BK / 8; ++j) {
+                    const uint64_t a_hi = sw64_desc(base + j * 32);
+                    const uint64_t a_lo = sw64_desc(base + kTileA + j * 32);
+                    const uint64_t b_hi = sw64_desc(base + 2 * kTileA + j * 32);
+                    const uint64_t b_lo = sw64_desc(base + 2 * kTileA + kTileB + j * 32);
+                    mma_tf32(tmem, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    mma_tf32(tmem, a_hi, b_lo, idesc, 1u);
+                    mma_tf32(tmem, a_hi, b_hi, idesc, 1u);
+                }
+                mma_commit(smem_u32(&empty[s]));
+            }
+            // arrives once every MMA of the tile has completed (also when cut short)
+            mma_commit(smem_u32(&tfull[0]));
+        }
+    } else {
+        // ------------------------------------ epilogue: partial -> shared memory
+        const int q = warp & 3;   // this warp's TMEM lane quarter
+        wait(smem_u32(&tfull[0]), 0);
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        float* dst = red + (size_t)(q * 32 + lane) * kRedLd;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4)
+                reinterpret_cast<float4*>(dst + c * 32)[i4] =
+                    make_float4(__uint_as_float(v[4 * i4]), __uint_as_float(v[4 * i4 + 1]),
+                                __uint_as_float(v[4 * i4 + 2]), __uint_as_float(v[4 * i4 + 3]));
+        }
+    }
+    __syncwarp();
+    // every partial of the cluster staged
+    cluster_sync_all();
+    grid_dep_wait();   // the residual input and the outputs belong to earlier kernels
+
+    // ---------------------------- rows [z R, (z + 1) R): sum in split order
+    const int R = BM / splits;
+    for (int idx = threadIdx.x; idx < R * (BN / 4); idx += THREADS) {
+        const int r = z * R + idx / (BN / 4), c4 = idx % (BN / 4);
+        const int row = m0 + r, col = n0 + 4 * c4;
+        if (row >= p.M || col >= p.N) continue;
+        const uint32_t local = smem_u32(red + (size_t)r * kRedLd + 4 * c4);
+        // every split's value in flight at once, then summed in split order
+        float4 v[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+            if (s < splits) v[s] = ld_cluster4(mapa_cluster(local, (uint32_t)s));
+        float4 acc = v[0];
+#pragma unroll
+        for (int s = 1; s < 8; ++s)
+            if (s < splits) {
+                acc.x = __fadd_rn(acc.x, v[s].x);
+                acc.y = __fadd_rn(acc.y, v[s].y);
+                acc.z = __fadd_rn(acc.z, v[s].z);
+                acc.w = __fadd_rn(acc.w, v[s].w);
+            }
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        const size_t o = (size_t)row * p.ldc + col;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (col + e >= p.N) break;
+            const float y = apply_epi<EPI>(a4[e], p.bias, col + e, p.C + o + e);
+            if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o + e] = y;
+            if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
+                const float h = tf32_hi(y);
+                p.C_hi[o + e] = h;
+                p.C_lo[o + e] = __fsub_rn(y, h);
+            }
+        }
+    }
+    // no CTA leaves while another may still read its shared memory
+    cluster_sync_all();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
     }
 }
 
@@ -455,20 +648,46 @@ cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStr
     return cudaGetLastError();
 }
 
+// Decode shapes: one cluster of `splits` CTAs per 128 x 128 tile (splits <= 8),
+// programmatic dependent launch.
+template <int EPI, int OUT>
+cudaError_t launch_split(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
+    CUtensorMap m[4];
+    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, BM) || !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, BM) ||
+        !make_map(&m[2], op.b_hi, a.N, a.K, op.ldb, 128) || !make_map(&m[3], op.b_lo, a.N, a.K, op.ldb, 128))
+        return cudaErrorInvalidValue;
+    constexpr size_t smem = split_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_split_kernel<EPI, OUT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    a.kb_per_split = (a.K / BK + splits - 1) / splits;
+    const int used = (a.K / BK + a.kb_per_split - 1) / a.kb_per_split;
+    a.splits = used;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(used, (a.N + 127) / 128, (a.M + BM - 1) / BM);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = used;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, tc_gemm_split_kernel<EPI, OUT>, m[0], m[1], m[2], m[3], a);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 template <int EPI, int OUT>
 cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
     if (splits <= 1) {
         a.kb_per_split = a.K / BK;
         return launch_bn<128, EPI, OUT>(op, a, 1, st);
     }
-    a.kb_per_split = (a.K / BK + splits - 1) / splits;
-    const int used = (a.K / BK + a.kb_per_split - 1) / a.kb_per_split;
-    cudaError_t e = launch_bn<128, EPI_STORE, TC_OUT_PARTIAL>(op, a, used, st);
-    if (e != cudaSuccess) return e;
-    const long long n = (long long)a.M * a.N;
-    const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 16);
-    tc_splitk_reduce<EPI, OUT><<<grid, 256, 0, st>>>(a, used);
-    return cudaGetLastError();
+    return launch_split<EPI, OUT>(op, a, splits, st);
 }
 
 }  // namespace
@@ -477,20 +696,22 @@ bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
     return M > 0 && N > 0 && K > 0 && K % BK == 0 && lda % 4 == 0 && ldb % 4 == 0 && encode_fn() != nullptr;
 }
 
-// Split count for a decode-sized matmul: enough blocks to cover the SMs,
-// chosen from N and K only.
+// Split count for a decode-sized matmul, chosen from N and K only, so that a
+// row's result never depends on how many rows are in the batch: the largest
+// power of two up to a portable cluster (8) with N tiles x splits <= 74, so
+// that two 128-row tiles (the largest decode batch) make one wave of CTAs,
+// and at least four 16-wide k-blocks per split.
 int tc_splits_for(int N, int K) {
     const int n_tiles = (N + 127) / 128;
     const int kb = K / BK;
     int s = 1;
-    while (n_tiles * s * 2 <= 148 && s * 2 <= kb / 4) s *= 2;
+    while (s < 8 && n_tiles * s * 2 <= 74 && s * 2 <= kb / 4) s *= 2;
     return s;
 }
 
 cudaError_t launch_tc_gemm(const TcOperands& op, const TcArgs& a, int epi, int out, int splits,
                            cudaStream_t st) {
     if (!tc_gemm_supported(a.M, a.N, a.K, op.lda, op.ldb)) return cudaErrorInvalidValue;
-    if (splits > 1 && !a.partial) return cudaErrorInvalidValue;
 #define TC_CASE(E, O) \
     if (epi == E && out == O) return launch_epi<E, O>(op, a, splits, st);
     TC_CASE(EPI_STORE, TC_OUT_F32)

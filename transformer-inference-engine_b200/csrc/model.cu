@@ -219,8 +219,6 @@ struct model {
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *ff = nullptr;
     float *xb_hi = nullptr, *xb_lo = nullptr, *attn_hi = nullptr, *attn_lo = nullptr;
     float *ff_hi = nullptr, *ff_lo = nullptr;
-    size_t partial_floats = 0;
-    float* d_partial = nullptr;  // split-K workspace of the decode matmuls
     int* d_err = nullptr;        // set by a kernel whose bounded wait expired
     size_t logit_rows = 0;
     float* logits = nullptr;
@@ -386,19 +384,6 @@ model_status ensure_slots(model* m, size_t B, int capacity) {
         m->am_parts = parts;
     }
     if ((rc = ensure_logits(m, B)) != MODEL_OK) return rc;
-    if (B > (size_t)kGemvRows) {
-        const int E = m->cfg.n_embd;
-        const int shapes[5][2] = {{3 * E, E}, {E, E}, {4 * E, E}, {E, 4 * E}, {m->cfg.vocab_size, E}};
-        size_t need_p = 0;
-        for (auto& sh : shapes) {
-            const int sp = tc_splits_for(sh[0], sh[1]);
-            if (sp > 1) need_p = std::max(need_p, (size_t)sp * B * (size_t)sh[0]);
-        }
-        if (need_p > m->partial_floats) {
-            drop_graphs(m);
-            if ((rc = grow(&m->d_partial, &m->partial_floats, need_p)) != MODEL_OK) return rc;
-        }
-    }
     return ensure_pinned(m, 2 * B + 16);
 }
 
@@ -417,7 +402,7 @@ model_status matmul(model* m, bool decode, int rows, Mat x, int ldx, Mat w, int 
     TcArgs a{};
     a.M = rows; a.N = N; a.K = K; a.bias = bias;
     a.C = y; a.C_hi = y_hi; a.C_lo = y_lo; a.ldc = ldy;
-    a.partial = m->d_partial; a.err = m->d_err;
+    a.err = m->d_err;
     const int out = y_hi ? (y ? TC_OUT_F32_HILO : TC_OUT_HILO) : TC_OUT_F32;
     const int splits = decode ? tc_splits_for(N, K) : 1;
     LAUNCH(launch_tc_gemm(op, a, epi, out, splits, st));
@@ -1090,7 +1075,6 @@ void model_free(model* m) {
     cudaFree(m->d_weights);
     cudaFree(m->d_split);
     cudaFree(m->x);  // the activation block (x, xb, qkv, attn, ff and their splits)
-    cudaFree(m->d_partial);
     cudaFree(m->d_err);
     cudaFree(m->logits); cudaFree(m->d_ids);
     cudaFree(m->d_tokens); cudaFree(m->d_lens); cudaFree(m->d_next); cudaFree(m->d_step);

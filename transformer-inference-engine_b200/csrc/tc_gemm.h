@@ -11,8 +11,7 @@ namespace tie {
 enum TcOut : int {
     TC_OUT_F32 = 0,       // C = y (fp32)
     TC_OUT_HILO = 1,      // C_hi, C_lo = the tf32 split of y (input of the next matmul)
-    TC_OUT_F32_HILO = 2,  // both
-    TC_OUT_PARTIAL = 3    // raw partial sums of one K split (internal)
+    TC_OUT_F32_HILO = 2   // both
 };
 
 // A = a_hi + a_lo: M x K rows of lda floats; B = b_hi + b_lo: N x K rows of ldb.
@@ -34,7 +33,6 @@ struct TcArgs {
     float* C_hi;             // [M, ldc] tf32-split outputs
     float* C_lo;
     int ldc;
-    float* partial;          // split-K workspace: splits x M x N floats
     int* err;                // device error flag (set when a bounded wait expires)
 };
 
