@@ -296,6 +296,10 @@ inline size_t step_sync_words(int n_layer) { return 5 * (size_t)n_layer + 1; }
 //   [step_trace_end(L) + 1 + i]   the producer has issued all of matrix i
 //                                 (4 per layer: qkv, proj, fc, mlp; then wte)
 __host__ __device__ inline int step_trace_end(int n_layer) { return 1 + 3 * (5 * n_layer + 1); }
-__host__ __device__ inline int step_trace_events(int n_layer) { return step_trace_end(n_layer) + 1 + 4 * n_layer + 1; }
+//   [step_trace_fine(L) + 16 k + 4 j + e]  layer 1, matrix k (qkv, proj, fc,
+//       mlp), ring packet j < 4: e = 0 loop top, 1 slot ready, 2 products
+//       done, 3 epilogue done (consumer thread 0)
+__host__ __device__ inline int step_trace_fine(int n_layer) { return step_trace_end(n_layer) + 1 + 4 * n_layer + 1; }
+__host__ __device__ inline int step_trace_events(int n_layer) { return step_trace_fine(n_layer) + 64; }
 
 }  // namespace tie

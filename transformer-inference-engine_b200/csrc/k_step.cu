@@ -8,16 +8,16 @@
 // release/acquire counter in global memory instead.
 //
 // Layout of a CTA (one per SM, all co-resident: cooperative launch):
-//   warp 0, lane 0   the producer. It walks the step's matrices in order (per
-//                    layer qkv, proj, fc, mlp; then wte for the head). For each
-//                    it first copies the stage's small parameters (LayerNorm
-//                    gain and shift, this CTA's slice of the bias) into one of
-//                    two parameter buffers, then streams this CTA's rows of the
-//                    matrix into a ring of 32 KB shared-memory slots. All copies
-//                    are bulk asynchronous copies (cp.async.bulk) completing on
-//                    an mbarrier per slot. Nothing it copies is computed in the
-//                    step, so it runs ahead of the consumers by the whole ring,
-//                    across stage boundaries.
+//   warp 0           the producer, two lanes. Lane 0 walks the step's
+//                    matrices in order (per layer qkv, proj, fc, mlp; then wte
+//                    for the head) and streams this CTA's rows of each into a
+//                    ring of 32 KB shared-memory slots; lane 1 copies each
+//                    stage's small parameters (LayerNorm gain and shift, this
+//                    CTA's slice of the bias) into one of two parameter
+//                    buffers. All copies are bulk asynchronous copies
+//                    (cp.async.bulk) completing on mbarriers. Nothing they copy
+//                    is computed in the step, so the weights run ahead of the
+//                    consumers by the whole ring, across stage boundaries.
 //   warps 1..7       the consumers. Per stage they wait for the stage's inputs
 //                    (a counter reaching its target), stage the activation rows
 //                    in shared memory (LayerNorm applied there where the stage
@@ -26,9 +26,9 @@
 //
 // Stages of layer l and what they wait for:
 //   A  LN1 + qkv (+ this step's K/V rows into the cache)    E of layer l-1
-//   B  attention: one unit per (sequence, head, 256 positions); a warp per
-//      16-position chunk; merged in the CTA, or by the last
-//      unit of a (sequence, head) when it spans several       A
+//   B  attention: one unit per (sequence, head, 16-position chunk),
+//      dealt to every consumer warp of the grid; merged by the
+//      warp completing a (sequence, head)                     A
 //   C  proj + residual                                       all merges of B
 //   D  LN2 + fc + gelu                                       C
 //   E  mlp + residual                                        D
@@ -59,7 +59,6 @@ constexpr int kRowsMax = 4;                     // sequences per step
 constexpr int D = 64;                           // head dim
 constexpr int PART = D + 2;                     // attention partial: max, sum, D sums
 constexpr int CHT = 16;                         // positions per attention chunk
-constexpr int kUnitChunks = 2 * kCons;          // chunks per attention unit (2 per warp)
 constexpr int kMaxPages = 64;
 constexpr int kMaxResid = 32;                   // residual columns a CTA keeps
 constexpr int kRegChunks = 6;                   // activation chunks per lane kept in registers (batch 1)
@@ -149,14 +148,17 @@ struct Smem {
     int lens[kRowsMax];
     int abort;
     int last;
-    alignas(16) float att[kUnitChunks][PART + 2];   // chunk partials of one attention unit
 };
 
 // ------------------------------------------------------------ the producer --
-__device__ void producer(const StepParams& p, Smem& sm, char* ring, float* params, const StepLayer* tab) {
+// Two lanes of warp 0, each its own sequence of bounded waits: lane 0 streams
+// the weight rows of every matrix in order through the ring, running ahead of
+// the consumers by the ring's whole depth; lane 1 copies each stage's small
+// parameters into the two parameter buffers as they free up. Neither waits on
+// the other.
+__device__ void producer_weights(const StepParams& p, Smem& sm, char* ring, const StepLayer* tab) {
     const uint64_t policy = evict_first_policy(), keep = evict_last_policy();
     const int n_mats = 4 * p.n_layer + 1, E = p.E;
-    const int pfl = param_floats(E, gridDim.x);
     // this CTA's rows of the tied head go into L2 a layer's share at a time:
     // the layers' stages wait on one another and leave HBM mostly idle
     const char* head0 = reinterpret_cast<const char*>(p.wte + (size_t)sm.r0[4] * E);
@@ -165,7 +167,6 @@ __device__ void producer(const StepParams& p, Smem& sm, char* ring, float* param
     const size_t pf_step = ((pf_total / p.n_layer) + 15) & ~(size_t)15;
     size_t pf_done = 0;
     uint32_t pk = 0;
-    int np = 0;   // parameter blocks issued
     bool ok = true;
     for (int i = 0; i < n_mats && ok; ++i) {
         const MatDesc d = mat_desc(p, tab, i);
@@ -176,9 +177,37 @@ __device__ void producer(const StepParams& p, Smem& sm, char* ring, float* param
                 bulk_prefetch_l2(head0 + pf_done + o, (uint32_t)min((size_t)32768, n - o), keep);
             pf_done += n;
         }
-        // the stage's parameters
+        const int g1 = r1 << d.lws;
+        for (int g = r0 << d.lws; g < g1; g += d.P, ++pk) {
+            const int slot = pk % p.slots;
+            const uint32_t par = (pk / p.slots) & 1;
+            if (sm.abort || !mbar_wait(&sm.empty[slot], par ^ 1)) { ok = false; break; }
+            const int ge = min(g + d.P, g1);
+            const size_t o0 = seg_off(d, g), o1 = seg_off(d, ge);
+            const uint32_t bytes = (uint32_t)((o1 - o0) * sizeof(float));
+            mbar_expect_tx(&sm.full[slot], bytes);
+            bulk_load(ring + (size_t)slot * kSlot, d.W + o0, bytes, &sm.full[slot], policy);
+        }
+        stamp(p, step_trace_end(p.n_layer) + 1 + i);
+    }
+    if (!ok) {
+        atomicExch(p.err, 1);
+        // let every copy still in flight land before the CTA's shared memory goes
+        const uint32_t n = pk < (uint32_t)p.slots ? pk : (uint32_t)p.slots;
+        for (uint32_t k = pk - n; k < pk; ++k) mbar_wait(&sm.full[k % p.slots], (k / p.slots) & 1);
+    }
+}
+
+__device__ void producer_params(const StepParams& p, Smem& sm, float* params, const StepLayer* tab) {
+    const int n_mats = 4 * p.n_layer + 1, E = p.E;
+    const int pfl = param_floats(E, gridDim.x);
+    int np = 0;   // parameter blocks issued
+    bool ok = true;
+    for (int i = 0; i < n_mats; ++i) {
+        const MatDesc d = mat_desc(p, tab, i);
+        const int r0 = sm.r0[d.kind], r1 = sm.r1[d.kind];
         const int ps = i & 1;
-        if (!mbar_wait(&sm.pempty[ps], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
+        if (sm.abort || !mbar_wait(&sm.pempty[ps], ((i >> 1) & 1) ^ 1)) { ok = false; break; }
         float* dst = params + (size_t)ps * pfl;
         const uint32_t ln_bytes = d.ln_g ? 2u * E * 4u : 0u;
         const int r0a = r0 & ~3, r1a = (r1 + 3) & ~3;
@@ -193,25 +222,9 @@ __device__ void producer(const StepParams& p, Smem& sm, char* ring, float* param
             if (b_bytes) bulk_load(dst + 2 * E, d.bias + r0a, b_bytes, &sm.pfull[ps]);
         }
         ++np;
-        // the stage's weight rows
-        const int g1 = r1 << d.lws;
-        for (int g = r0 << d.lws; g < g1; g += d.P, ++pk) {
-            const int slot = pk % p.slots;
-            const uint32_t par = (pk / p.slots) & 1;
-            if (!mbar_wait(&sm.empty[slot], par ^ 1)) { ok = false; break; }
-            const int ge = min(g + d.P, g1);
-            const size_t o0 = seg_off(d, g), o1 = seg_off(d, ge);
-            const uint32_t bytes = (uint32_t)((o1 - o0) * sizeof(float));
-            mbar_expect_tx(&sm.full[slot], bytes);
-            bulk_load(ring + (size_t)slot * kSlot, d.W + o0, bytes, &sm.full[slot], policy);
-        }
-        stamp(p, step_trace_end(p.n_layer) + 1 + i);
     }
     if (!ok) {
         atomicExch(p.err, 1);
-        // let every copy still in flight land before the CTA's shared memory goes
-        const uint32_t n = pk < (uint32_t)p.slots ? pk : (uint32_t)p.slots;
-        for (uint32_t k = pk - n; k < pk; ++k) mbar_wait(&sm.full[k % p.slots], (k / p.slots) & 1);
         for (int j = max(0, np - 2); j < np; ++j) mbar_wait(&sm.pfull[j & 1], (j >> 1) & 1);
     }
 }
@@ -401,11 +414,16 @@ __device__ bool stage_matmul(const StepParams& p, Smem& sm, const StepLayer* tab
             xr[u] = 32 * u + lane < nc ? reinterpret_cast<const float4*>(xs)[c0 + 32 * u + lane]
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int g = r0 << d.lws; g < g1; g += d.P, ++pk) {
+    const bool fine = p.trace && t == 0 && layer == 1;
+    const int fine0 = step_trace_fine(p.n_layer) + 16 * (mi & 3);
+    int pkt = 0;
+    for (int g = r0 << d.lws; g < g1; g += d.P, ++pk, ++pkt) {
         const int slot = pk % p.slots;
         const uint32_t par = (pk / p.slots) & 1;
         const int ge = min(g + d.P, g1);
         const int gs = g + warp;   // this warp's segment
+        const bool fs = fine && pkt < 4;
+        if (fs) stamp(p, fine0 + 4 * pkt);
         float acc[kRowsMax] = {0.f, 0.f, 0.f, 0.f};
         bool have = false;
         if (gs < ge && !sm.abort) {
@@ -414,6 +432,7 @@ __device__ bool stage_matmul(const StepParams& p, Smem& sm, const StepLayer* tab
                 sm.abort = 1;
             } else {
                 have = true;
+                if (fs) stamp(p, fine0 + 4 * pkt + 1);
                 const float* w = reinterpret_cast<const float*>(ring + (size_t)slot * kSlot) +
                                  (seg_off(d, gs) - seg_off(d, g));
                 const int s = gs & (WS - 1);
@@ -460,6 +479,7 @@ __device__ bool stage_matmul(const StepParams& p, Smem& sm, const StepLayer* tab
             }
         }
         __syncwarp();
+        if (fs) stamp(p, fine0 + 4 * pkt + 2);
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
         if (WS == 1) {
             if (have && lane < M) epilogue<KIND>(p, sm, layer, pick(acc, lane), gs, lane, bias, r0a, best);
@@ -478,6 +498,7 @@ __device__ bool stage_matmul(const StepParams& p, Smem& sm, const StepLayer* tab
             }
             cons_sync();
         }
+        if (fs) stamp(p, fine0 + 4 * pkt + 3);
     }
     cons_sync();
     return !sm.abort;
@@ -541,70 +562,78 @@ __device__ void attn_chunk(const StepParams& p, const Smem& sm, const float* kl,
     if (lane == 0) { out[0] = mx; out[1] = l; }
 }
 
-// Attention of layer `layer`: units of (sequence, head, up to 16 chunks), one
-// per CTA at a time. Merged heads count on `ctr`.
+// Attention of layer `layer`: one unit per (sequence, head, 16-position
+// chunk), dealt round-robin to every consumer warp of the grid (unit u: CTA
+// u % G, warp (u / G) % kCons), so a batch-1 step spreads its chunks over the
+// whole GPU. Each warp writes its chunk partial; the warp that completes a
+// (sequence, head)'s count merges the partials in chunk order (the merge of
+// attn_decode_fused_kernel<16>), writes the head's 64 outputs and counts the
+// head on `ctr`.
 __device__ void stage_attention(const StepParams& p, Smem& sm, int layer, unsigned* ctr) {
     const int t = threadIdx.x - 32, warp = t >> 5, lane = t & 31;
-    const int H = p.H, E = p.E;
-    int gmax = 0;
-    for (int m = 0; m < p.M; ++m) {
-        const int ns = (sm.lens[m] + CHT) / CHT;
-        gmax = max(gmax, (ns + kUnitChunks - 1) / kUnitChunks);
-    }
-    const int units = p.M * H * gmax;
+    const int H = p.H, E = p.E, G = gridDim.x;
+    // units per sequence: H x its chunks; offsets by a scan over the (<= 4) sequences
+    int off[kRowsMax + 1];
+    off[0] = 0;
+    for (int m = 0; m < p.M; ++m) off[m + 1] = off[m] + H * ((sm.lens[m] + CHT) / CHT);
+    const int units = off[p.M];
     const float* kl = p.k + (size_t)layer * p.layer_stride;
     const float* vl = p.v + (size_t)layer * p.layer_stride;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        const int grp = u % gmax, h = (u / gmax) % H, b = u / (gmax * H);
-        const int ctx = sm.lens[b] + 1;
-        const int ns = (ctx + CHT - 1) / CHT;
-        const int ng = (ns + kUnitChunks - 1) / kUnitChunks;
-        if (grp >= ng) continue;   // uniform over the CTA
-        const int c_lo = grp * kUnitChunks, c_hi = min(ns, c_lo + kUnitChunks);
+    for (int u = warp * G + blockIdx.x; u < units; u += G * kCons) {
+        int b = 0;
+        while (u >= off[b + 1]) ++b;
+        const int ctx = sm.lens[b] + 1, ns = (ctx + CHT - 1) / CHT;
+        const int r = u - off[b], h = r / ns, c = r - h * ns;
         float4 qv[8];
         const float* qp = p.qkv + (size_t)b * 3 * E + h * D;
 #pragma unroll
         for (int j = 0; j < 8; ++j) qv[j] = ld_cg4(qp + 4 * (2 * j + (lane & 1)));
-        for (int c = c_lo + warp; c < c_hi; c += kCons) {
-            const int p0 = c * CHT;
-            attn_chunk(p, sm, kl, vl, b, h, p0, min(CHT, ctx - p0), qv, lane, sm.att[c - c_lo]);
+        float* part_g = p.part + (size_t)(b * H + h) * p.max_splits * PART;
+        const int p0 = c * CHT;
+        attn_chunk(p, sm, kl, vl, b, h, p0, min(CHT, ctx - p0), qv, lane, part_g + (size_t)c * PART);
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(&p.head_cnt[b * H + h]) : "memory");
+            last = old == ns - 1;
         }
-        cons_sync();
-        const float* part_g = p.part + (size_t)(b * H + h) * p.max_splits * PART;
-        bool merge = true;
-        if (ng > 1) {
-            // this unit's partials to global; the last unit of the head merges
-            float* dst = p.part + (size_t)(b * H + h) * p.max_splits * PART + (size_t)c_lo * PART;
-            for (int i = t; i < (c_hi - c_lo) * PART; i += kCons * 32) dst[i] = sm.att[i / PART][i % PART];
-            __threadfence();
-            cons_sync();
-            if (t == 0) sm.last = atomicAdd(&p.head_cnt[b * H + h], 1) == ng - 1;
-            cons_sync();
-            merge = sm.last;
-            if (merge) __threadfence();
-        }
-        if (merge) {
-            if (t < D) {
-                auto P = [&](int k, int f) {
-                    return ng > 1 ? __ldcg(part_g + (size_t)k * PART + f) : sm.att[k][f];
-                };
-                float mm = P(0, 0);
-                for (int k = 1; k < ns; ++k) mm = fmaxf(mm, P(k, 0));
-                float lt = 0.f, o = 0.f;
-                for (int k = 0; k < ns; ++k) {
-                    const float cf = expf(P(k, 0) - mm);
-                    lt = fmaf(P(k, 1), cf, lt);
-                    o = fmaf(P(k, 2 + t), cf, o);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __syncwarp();   // lane 0 acquired the other warps' partials for the whole warp
+        float mm = -INFINITY;
+        for (int k = lane; k < ns; k += 32) mm = fmaxf(mm, __ldcg(part_g + (size_t)k * PART));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        float lt = 0.f, o0 = 0.f, o1 = 0.f;
+        for (int k0 = 0; k0 < ns; k0 += 32) {
+            float2 ml = make_float2(0.f, 0.f);
+            if (k0 + lane < ns) ml = ld_cg2(part_g + (size_t)(k0 + lane) * PART);
+            const int kn = min(32, ns - k0);
+            for (int k1 = 0; k1 < kn; k1 += 8) {
+                float2 ov[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k1 + k < kn) ov[k] = ld_cg2(part_g + (size_t)(k0 + k1 + k) * PART + 2 + 2 * lane);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float mk = __shfl_sync(0xffffffffu, ml.x, (k1 + k) & 31);
+                    const float lk = __shfl_sync(0xffffffffu, ml.y, (k1 + k) & 31);
+                    if (k1 + k < kn) {
+                        const float cf = expf(mk - mm);
+                        lt = fmaf(lk, cf, lt);
+                        o0 = fmaf(ov[k].x, cf, o0);
+                        o1 = fmaf(ov[k].y, cf, o1);
+                    }
                 }
-                p.attn[(size_t)b * E + h * D + t] = o / lt;
-            }
-            cons_sync();
-            if (t == 0) {
-                if (ng > 1) p.head_cnt[b * H + h] = 0;
-                signal(ctr);
             }
         }
-        cons_sync();
+        *reinterpret_cast<float2*>(p.attn + (size_t)b * E + h * D + 2 * lane) = make_float2(o0 / lt, o1 / lt);
+        __syncwarp();
+        if (lane == 0) {
+            p.head_cnt[b * H + h] = 0;
+            signal(ctr);
+        }
     }
 }
 
@@ -790,7 +819,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepParams p) {
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-        if (threadIdx.x == 0) producer(p, sm, ring, params, tab);
+        if (threadIdx.x == 0) producer_weights(p, sm, ring, tab);
+        else if (threadIdx.x == 1) producer_params(p, sm, params, tab);
         return;
     }
     consumers(p, sm, tab, ring, xs, params);
