@@ -214,7 +214,8 @@ cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const fl
                             const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
                             int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st, int wt = WF_F32,
                             const void* wq = nullptr, const float* scale = nullptr);
-int dec_head_blocks(int V, int K, int wt = WF_F32);
+int dec_head_blocks(int V, int K, int wt, int M);
+int dec_head_blocks_max(int V, int K);
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
                             int* part_idx, cudaStream_t st, int wt = WF_F32, const void* wq = nullptr,

@@ -1,23 +1,26 @@
-// k_decode.cu -- the small-batch decode step (at most 16 sequences), fused and
+// k_decode.cu -- the small-batch decode matmuls (at most 16 sequences),
 // chained with programmatic dependent launch.
 //
 // A decode step at batch 1 moves ~0.5 GB of fp32 weights through a few dozen
 // matmuls whose individual transfers take ~1 us at HBM speed, so the step is
 // bound by the gaps between kernels as much as by bandwidth. Two measures:
 //
-//   * fusion: LayerNorm runs inside the matmul that consumes it (every block
-//     normalises the <= 16 input rows itself, in shared memory, with the same
-//     double-precision statistics as the standalone kernel), the K/V rows of a
-//     step are stored by the QKV matmul's epilogue, and LN_f runs inside the
-//     tied head;
+//   * fusion: the K/V rows of a step are stored by the QKV matmul's epilogue,
+//     bias, GELU and the residual add run in the epilogues, and the tied head
+//     keeps a running greedy argmax (LayerNorm runs once per row before the
+//     matmul that consumes it, in layernorm_kernel);
 //   * programmatic dependent launch: every kernel first issues the loads of its
 //     own weight rows (which no earlier kernel writes), then lets the next
 //     kernel launch (griddepcontrol.launch_dependents), and only then waits for
 //     its predecessor's results (griddepcontrol.wait). Weight streaming thus
 //     overlaps the previous kernel's tail and the launch latency.
 //
-// Each warp holds all of its weight chunks in registers (loaded before the
-// dependency wait), so a matrix is in flight in one round trip.
+// Each warp holds all of its weight chunks of a row group in registers (loaded
+// before the dependency wait), so a matrix is in flight in one round trip. The
+// kernel is compiled per row bucket (1, 2, 4, 8 or 16 activation rows), so its
+// accumulators, registers and code are those of the batch it runs.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tie {
@@ -25,7 +28,6 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kMaxRows = 16;
-constexpr int kStageFloats = 0;               // activation rows copied to shared memory up to this many floats (0: read through L1)
 
 __device__ __forceinline__ float4 ld_stream(const float* p) {
     float4 v;
@@ -35,36 +37,9 @@ __device__ __forceinline__ float4 ld_stream(const float* p) {
     return v;
 }
 
-// LayerNorm of rows [0, M) of x (row stride ldx) into xs (row stride K), the
-// arithmetic of layernorm_kernel (k_misc.cu). Each row is first copied into
-// xs with all of the block's 16-byte loads in flight; the statistics (one warp
-// per row, the canonical order of ln_stats_warp) and the normalisation then
-// run out of shared memory, in place.
-__device__ void ln_rows_to_smem(const float* __restrict__ x, int ldx, const float* __restrict__ g,
-                                const float* __restrict__ b, float eps, int M, int K, float* xs) {
-    const int K4 = K >> 2;
-    for (int i = threadIdx.x; i < M * K4; i += kWarps * 32) {
-        const int m = i / K4, c = i % K4;
-        reinterpret_cast<float4*>(xs + (size_t)m * K)[c] =
-            __ldg(reinterpret_cast<const float4*>(x + (size_t)m * ldx) + c);
-    }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = warp; m < M; m += kWarps) {
-        float* xr = xs + (size_t)m * K;
-        double mean;
-        float inv;
-        ln_stats_warp(xr, K, eps, lane, mean, inv);
-        for (int i = lane; i < K; i += 32) xr[i] = ln_apply(xr[i], mean, inv, g[i], b[i]);
-    }
-}
-
 struct DecArgs {
-    const float* x;   // input rows [M][ldx] (pre-normalisation when LN)
+    const float* x;   // input rows [M][ldx]
     int ldx;
-    const float* ln_g;
-    const float* ln_b;
-    float eps;
     const float* W;   // [N][K], K-major (fp32)
     const void* Wq;   // [N][K] bf16 or int8 (reduced weight formats)
     const float* scale;   // [N] int8 per-row scales
@@ -90,8 +65,8 @@ __device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
 // cut into WS slices of K / WS and each warp owns RPW rows of one slice. A warp
 // loads ALL of its weight chunks (at most CPL 16-byte chunks per lane per row)
 // into registers before the dependency wait, so the whole matrix is in flight
-// at once; after the wait it only reads the <= 16 activation rows (shared
-// memory when normalised here, else global through L1) and reduces.
+// at once; after the wait it only reads the activation rows (through L1) and
+// reduces.
 // Per (row, activation row) the sum is: within a slice, lane c accumulates
 // chunks c, c + 32, ... (four FMAs per chunk, in order), then an xor-butterfly
 // across lanes; the WS slice sums are added in slice order. The order depends
@@ -115,17 +90,17 @@ __device__ __forceinline__ float chunk_elem(const float4& c, int e) {
     }
 }
 
-// The kernel is persistent: a block normalises (or stages) the activation
-// rows once and then walks row groups blockIdx.x, + gridDim.x, ... The first
-// group's weights are loaded before the dependency wait; each later group's
-// are loaded while the previous group's sums are finished.
-template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
+// The kernel is persistent (one wave: the grid is what fits on the GPU at
+// once) and walks row groups blockIdx.x, + gridDim.x, ... The first group's
+// weights are loaded before the dependency wait; each later group's are
+// loaded while the previous group's sums are finished. MB is the row bucket:
+// a.M <= MB activation rows.
+template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>
 __global__ void __launch_bounds__(kWarps * 32)
 dec_gemv_kernel(DecArgs a) {
-    extern __shared__ __align__(16) float xs[];  // [M][K] when LN
     constexpr int GROUPS = kWarps / WS;          // row groups per block
     constexpr int RPB = GROUPS * RPW;            // rows per block iteration
-    __shared__ float s_part[GROUPS][WS][RPW][kMaxRows];
+    __shared__ float s_part[GROUPS][WS][RPW][MB];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = warp / WS, ks = warp % WS;
     constexpr int EPC = elems_per_chunk<WT>();
@@ -157,27 +132,8 @@ dec_gemv_kernel(DecArgs a) {
     pdl_trigger();
     pdl_wait();
 
-    // 2. the activation rows, once per block: normalised into shared memory,
-    //    or copied there when they fit (kStageFloats), else read through L1
     const float* X = a.x;
-    int ldx = a.ldx;
-    const bool staged = LN || a.M * a.K <= kStageFloats;
-    if constexpr (LN) {
-        ln_rows_to_smem(a.x, a.ldx, a.ln_g, a.ln_b, a.eps, a.M, a.K, xs);
-        __syncthreads();
-        X = xs;
-        ldx = a.K;
-    } else if (staged) {
-        const int K4x = a.K >> 2;
-        for (int i = threadIdx.x; i < a.M * K4x; i += kWarps * 32) {
-            const int m = i / K4x, c = i - m * K4x;
-            reinterpret_cast<float4*>(xs + (size_t)m * a.K)[c] =
-                __ldg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx) + c);
-        }
-        __syncthreads();
-        X = xs;
-        ldx = a.K;
-    }
+    const int ldx = a.ldx;
 
     // head: this block's best (value, index) per activation row, over all its rows
     float bv = 0.f;
@@ -187,25 +143,23 @@ dec_gemv_kernel(DecArgs a) {
     for (int blk = blockIdx.x; blk * RPB < n_iter_rows; blk += gridDim.x) {
         const int row0 = (blk * GROUPS + grp) * RPW;
         // 3. slice sums
-        float acc[RPW][kMaxRows];
+        float acc[RPW][MB];
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
-            for (int m = 0; m < kMaxRows; ++m) acc[r][m] = 0.f;
+            for (int m = 0; m < MB; ++m) acc[r][m] = 0.f;
 #pragma unroll
         for (int u = 0; u < CPL; ++u) {
             const int c = c0 + u * 32 + lane;
             if (c < c1) {
                 if constexpr (WT == 0 && RPW == 1 && WS == 1 && CPL <= 8) {
                     // every row's activation chunk first, then the sums
-                    float4 xv[kMaxRows];
+                    float4 xv[MB];
 #pragma unroll
-                    for (int m = 0; m < kMaxRows; ++m)
-                        if (m < a.M)
-                            xv[m] = staged ? *reinterpret_cast<const float4*>(X + (size_t)m * ldx + 4 * c)
-                                           : __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
+                    for (int m = 0; m < MB; ++m)
+                        if (m < a.M) xv[m] = __ldg(reinterpret_cast<const float4*>(X + (size_t)m * ldx) + c);
 #pragma unroll
-                    for (int m = 0; m < kMaxRows; ++m) {
+                    for (int m = 0; m < MB; ++m) {
                         if (m < a.M) {
 #pragma unroll
                             for (int r = 0; r < RPW; ++r) {
@@ -220,15 +174,14 @@ dec_gemv_kernel(DecArgs a) {
                     }
                 } else {
 #pragma unroll
-                for (int m = 0; m < kMaxRows; ++m) {
+                for (int m = 0; m < MB; ++m) {
                     if (m < a.M) {
                         {
 #pragma unroll
                             for (int q4 = 0; q4 < EPC / 4; ++q4) {
                                 // (fp32: EPC / 4 == 1 and chunk_elem is the float4's lanes)
                                 const float* xp = X + (size_t)m * ldx + (size_t)c * EPC + 4 * q4;
-                                const float4 xv = staged ? *reinterpret_cast<const float4*>(xp)
-                                                         : __ldg(reinterpret_cast<const float4*>(xp));
+                                const float4 xv = __ldg(reinterpret_cast<const float4*>(xp));
 #pragma unroll
                                 for (int r = 0; r < RPW; ++r) {
                                     float t = acc[r][m];
@@ -250,7 +203,7 @@ dec_gemv_kernel(DecArgs a) {
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
-            for (int m = 0; m < kMaxRows; ++m) {
+            for (int m = 0; m < MB; ++m) {
                 if (m >= a.M) break;  // uniform across the block
                 float v = acc[r][m];
 #pragma unroll
@@ -261,7 +214,7 @@ dec_gemv_kernel(DecArgs a) {
 #pragma unroll
             for (int r = 0; r < RPW; ++r)
 #pragma unroll
-                for (int m = 0; m < kMaxRows; ++m) s_part[grp][ks][r][m] = acc[r][m];
+                for (int m = 0; m < MB; ++m) s_part[grp][ks][r][m] = acc[r][m];
         }
         __syncthreads();
 
@@ -323,125 +276,159 @@ dec_gemv_kernel(DecArgs a) {
     }
 }
 
-// Blocks of a launch: one per row group up to four per SM; the kernel walks
-// the remaining groups itself.
-int gemv_grid(int N, int rows_per_block) {
-    static int cap = 0;
-    if (!cap) {
-        int dev = 0, sms = 148;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
-                                                      cudaSuccess) {
+// Blocks of a launch: one per row group, up to what fits on the GPU at once
+// (the kernel's occupancy, so the persistent grid is one wave); the kernel
+// walks the remaining groups itself.
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
+                                                      cudaSuccess || n <= 0) {
             cudaGetLastError();
-            sms = 148;
+            n = 148;
         }
-        cap = 4 * sms;
     }
-    const int need = (N + rows_per_block - 1) / rows_per_block;
-    return need < cap ? need : cap;
+    return n;
 }
 
-template <int EPI, bool LN, int RPW, int WS, int CPL, int WT = 0>
-cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
-    // the kernel stages the activation rows whenever it normalises them or
-    // they fit kStageFloats; that is exactly when it needs this much
-    const bool staged = LN || a.M * a.K <= kStageFloats;
-    const size_t smem = staged ? (size_t)a.M * a.K * sizeof(float) : 0;
-    auto k = dec_gemv_kernel<EPI, LN, RPW, WS, CPL, WT>;
-    if (smem > 32 * 1024) {   // with the static shared memory, beyond the default 48 KB
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
+template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>
+int resident_blocks() {
+    static int per_sm = 0;
+    if (!per_sm) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dec_gemv_kernel<EPI, MB, RPW, WS, CPL, WT>,
+                                                          kWarps * 32, 0) != cudaSuccess || per_sm <= 0) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
     }
+    return per_sm * sm_count();
+}
+
+template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>
+cudaError_t dec_launch(const DecArgs& a, cudaStream_t st) {
     constexpr int rows_per_block = (kWarps / WS) * RPW;
-    const int grid = gemv_grid(a.N, rows_per_block);
-    cudaError_t e = launch_pdl(k, dim3(grid), dim3(kWarps * 32), smem, st, a);
+    const int need = (a.N + rows_per_block - 1) / rows_per_block;
+    const int grid = std::min(need, resident_blocks<EPI, MB, RPW, WS, CPL, WT>());
+    cudaError_t e = launch_pdl(dec_gemv_kernel<EPI, MB, RPW, WS, CPL, WT>, dim3(grid), dim3(kWarps * 32), 0, st, a);
     return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// The row bucket of M activation rows
+template <int EPI, int RPW, int WS, int CPL, int WT>
+cudaError_t dec_launch_m(const DecArgs& a, cudaStream_t st) {
+    if (a.M <= 1) return dec_launch<EPI, 1, RPW, WS, CPL, WT>(a, st);
+    if (a.M <= 2) return dec_launch<EPI, 2, RPW, WS, CPL, WT>(a, st);
+    if (a.M <= 4) return dec_launch<EPI, 4, RPW, WS, CPL, WT>(a, st);
+    if (a.M <= 8) return dec_launch<EPI, 8, RPW, WS, CPL, WT>(a, st);
+    return dec_launch<EPI, 16, RPW, WS, CPL, WT>(a, st);
 }
 
 // The slicing of K for a matrix: each lane holds at most 8 chunks per row.
 //   at most 256 chunks per row: whole rows, WS = 1
 //   at most 1024: WS = 4; at most 2048 (fp32 only): WS = 4 with 16 chunks per lane
-template <int EPI, bool LN, int WT>
+template <int EPI, int WT>
 cudaError_t dec_dispatch(const DecArgs& a, cudaStream_t st) {
     const int KC = a.K / elems_per_chunk<WT>();
-    if (KC <= 256) return dec_launch<EPI, LN, 1, 1, 8, WT>(a, st);
-    if (KC <= 1024) return dec_launch<EPI, LN, 1, 4, 8, WT>(a, st);
+    if (KC <= 256) return dec_launch_m<EPI, 1, 1, 8, WT>(a, st);
+    if (KC <= 1024) return dec_launch_m<EPI, 1, 4, 8, WT>(a, st);
     if constexpr (WT == 0)
-        if (KC <= 2048) return dec_launch<EPI, LN, 1, 4, 16, WT>(a, st);
+        if (KC <= 2048) return dec_launch_m<EPI, 1, 4, 16, WT>(a, st);
     return cudaErrorInvalidValue;
 }
 
-template <int EPI, int WT>
-cudaError_t dec_dispatch_ln(const DecArgs& a, bool ln, cudaStream_t st) {
-    return ln ? dec_dispatch<EPI, true, WT>(a, st) : dec_dispatch<EPI, false, WT>(a, st);
-}
-
 template <int WT>
-cudaError_t dec_dispatch_epi(const DecArgs& a, int epi, bool ln, cudaStream_t st) {
+cudaError_t dec_dispatch_epi(const DecArgs& a, int epi, cudaStream_t st) {
     switch (epi) {
-        case EPI_BIAS: return dec_dispatch_ln<DEC_BIAS, WT>(a, ln, st);
-        case EPI_BIAS_GELU: return dec_dispatch_ln<DEC_BIAS_GELU, WT>(a, ln, st);
-        case EPI_BIAS_RESID: return dec_dispatch_ln<DEC_BIAS_RESID, WT>(a, ln, st);
-        case EPI_QKV_KV: return dec_dispatch_ln<DEC_QKV_KV, WT>(a, ln, st);
+        case EPI_BIAS: return dec_dispatch<DEC_BIAS, WT>(a, st);
+        case EPI_BIAS_GELU: return dec_dispatch<DEC_BIAS_GELU, WT>(a, st);
+        case EPI_BIAS_RESID: return dec_dispatch<DEC_BIAS_RESID, WT>(a, st);
+        case EPI_QKV_KV: return dec_dispatch<DEC_QKV_KV, WT>(a, st);
     }
     return cudaErrorInvalidValue;
 }
 
 template <int WT>
-cudaError_t head_dispatch(const DecArgs& a, bool ln, cudaStream_t st) {
+cudaError_t head_dispatch(const DecArgs& a, cudaStream_t st) {
     const int KC = a.K / elems_per_chunk<WT>();
-    if (KC <= 256)
-        return ln ? dec_launch<DEC_HEAD, true, 4, 1, 8, WT>(a, st) : dec_launch<DEC_HEAD, false, 4, 1, 8, WT>(a, st);
-    if (KC <= 1024)
-        return ln ? dec_launch<DEC_HEAD, true, 1, 4, 8, WT>(a, st) : dec_launch<DEC_HEAD, false, 1, 4, 8, WT>(a, st);
+    if (KC <= 256) return dec_launch_m<DEC_HEAD, 4, 1, 8, WT>(a, st);
+    if (KC <= 1024) return dec_launch_m<DEC_HEAD, 1, 4, 8, WT>(a, st);
     return cudaErrorInvalidValue;
 }
 
 int chunk_elems(int wt) { return wt == 0 ? 4 : (wt == 1 ? 8 : 16); }
 
-}  // namespace
-
-// Rows per head block: 4 rows in each of 4 warps while a row is at most 256
-// chunks (RPW 4, WS 1), else one row cut into 4 slices (RPW 1, WS 4).
-int dec_head_blocks(int V, int K, int wt) {
-    const int rows = K / chunk_elems(wt) <= 256 ? kWarps * 4 : 1;
-    return gemv_grid(V, rows);
+// Blocks of the tied head's launch for M rows (one partial best per block
+// and row): 4 rows in each of 4 warps while a row is at most 256 chunks
+// (RPW 4, WS 1), else one row cut into 4 slices (RPW 1, WS 4).
+template <int WT>
+int head_blocks_wt(int V, int K, int M) {
+    const bool whole = K / elems_per_chunk<WT>() <= 256;
+    const int rows = whole ? kWarps * 4 : 1;
+    const int need = (V + rows - 1) / rows;
+    int cap;
+    if (whole) {
+        cap = M <= 1 ? resident_blocks<DEC_HEAD, 1, 4, 1, 8, WT>() : M <= 2 ? resident_blocks<DEC_HEAD, 2, 4, 1, 8, WT>()
+            : M <= 4 ? resident_blocks<DEC_HEAD, 4, 4, 1, 8, WT>() : M <= 8 ? resident_blocks<DEC_HEAD, 8, 4, 1, 8, WT>()
+            : resident_blocks<DEC_HEAD, 16, 4, 1, 8, WT>();
+    } else {
+        cap = M <= 1 ? resident_blocks<DEC_HEAD, 1, 1, 4, 8, WT>() : M <= 2 ? resident_blocks<DEC_HEAD, 2, 1, 4, 8, WT>()
+            : M <= 4 ? resident_blocks<DEC_HEAD, 4, 1, 4, 8, WT>() : M <= 8 ? resident_blocks<DEC_HEAD, 8, 1, 4, 8, WT>()
+            : resident_blocks<DEC_HEAD, 16, 1, 4, 8, WT>();
+    }
+    return std::min(need, cap);
 }
 
-// y = [LN](x) . W^T (+ epilogue) for M <= 16 rows, chained with PDL. Weights
-// fp32 (W), or with wt 1 / 2 bf16 / int8 (wq, int8 with per-row scales).
+}  // namespace
+
+// Blocks (one partial best per block and row) of the tied head's launch for
+// M rows; and the most any row count or weight format uses (buffer sizing).
+int dec_head_blocks(int V, int K, int wt, int M) {
+    return wt == 1 ? head_blocks_wt<1>(V, K, M) : wt == 2 ? head_blocks_wt<2>(V, K, M) : head_blocks_wt<0>(V, K, M);
+}
+
+int dec_head_blocks_max(int V, int K) {
+    int n = 0;
+    for (int wt : {0, 1, 2})
+        for (int M : {1, 2, 4, 8, 16}) n = std::max(n, dec_head_blocks(V, K, wt, M));
+    return n;
+}
+
+// y = x . W^T (+ epilogue) for M <= 16 rows, chained with PDL. Weights fp32
+// (W), or with wt 1 / 2 bf16 / int8 (wq, int8 with per-row scales).
 cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, const float* bias, float* y, int ldy, int M, int N, int K,
                             int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st, int wt,
                             const void* wq, const float* scale) {
+    (void)eps;
     if (M <= 0 || M > kMaxRows || (ldx & 3) || wt < 0 || wt > 2 || K % chunk_elems(wt)) return cudaErrorInvalidValue;
+    if (ln_g || ln_b) return cudaErrorInvalidValue;   // LayerNorm runs in layernorm_kernel
     if ((wt != 0 && !wq) || (wt == 2 && !scale)) return cudaErrorInvalidValue;
     if (epi == EPI_QKV_KV && (!kv || !lens)) return cudaErrorInvalidValue;
     DecArgs a{};
-    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W; a.bias = bias;
+    a.x = x; a.ldx = ldx; a.W = W; a.bias = bias;
     a.Wq = wq; a.scale = scale;
     a.y = y; a.ldy = ldy; a.M = M; a.N = N; a.K = K;
     if (kv) a.kv = *kv;
     a.lens = lens;
-    const bool ln = ln_g != nullptr;
-    if (wt == 1) return dec_dispatch_epi<1>(a, epi, ln, st);
-    if (wt == 2) return dec_dispatch_epi<2>(a, epi, ln, st);
-    return dec_dispatch_epi<0>(a, epi, ln, st);
+    if (wt == 1) return dec_dispatch_epi<1>(a, epi, st);
+    if (wt == 2) return dec_dispatch_epi<2>(a, epi, st);
+    return dec_dispatch_epi<0>(a, epi, st);
 }
 
-// The tied head with LN_f in its prologue: logits (optional) and per-block
-// partial maxima for launch_argmax_finalize.
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,
                             int* part_idx, cudaStream_t st, int wt, const void* wq, const float* scale) {
+    (void)eps;
     if (M <= 0 || M > kMaxRows || (ldx & 3) || wt < 0 || wt > 2 || K % chunk_elems(wt)) return cudaErrorInvalidValue;
+    if (ln_g || ln_b) return cudaErrorInvalidValue;   // LN_f runs in layernorm_kernel
     if ((wt != 0 && !wq) || (wt == 2 && !scale)) return cudaErrorInvalidValue;
     DecArgs a{};
-    a.x = x; a.ldx = ldx; a.ln_g = ln_g; a.ln_b = ln_b; a.eps = eps; a.W = W; a.Wq = wq; a.scale = scale;
+    a.x = x; a.ldx = ldx; a.W = W; a.Wq = wq; a.scale = scale;
     a.y = logits; a.ldy = ldl; a.M = M; a.N = V; a.K = K; a.part_val = part_val; a.part_idx = part_idx;
-    const bool ln = ln_g != nullptr;
-    if (wt == 1) return head_dispatch<1>(a, ln, st);
-    if (wt == 2) return head_dispatch<2>(a, ln, st);
-    return head_dispatch<0>(a, ln, st);
+    if (wt == 1) return head_dispatch<1>(a, st);
+    if (wt == 2) return head_dispatch<2>(a, st);
+    return head_dispatch<0>(a, st);
 }
 
 }  // namespace tie

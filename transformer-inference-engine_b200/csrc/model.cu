@@ -375,7 +375,7 @@ model_status ensure_slots(model* m, size_t B, int capacity) {
     int sms = 0;
     CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device));
     const size_t parts = (size_t)std::max({gemv_argmax_blocks(m->cfg.vocab_size),
-                                           dec_head_blocks(m->cfg.vocab_size, m->cfg.n_embd), sms}) * B;
+                                           dec_head_blocks_max(m->cfg.vocab_size, m->cfg.n_embd), sms}) * B;
     if (parts > m->am_parts) {
         drop_graphs(m);
         size_t c1 = m->am_parts, c2 = m->am_parts;
@@ -599,7 +599,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
         LAUNCH(launch_layernorm(m->x, m->lnf_w, m->lnf_b, m->xb, B, E, eps, st));
         LAUNCH(launch_dec_head(m->xb, E, nullptr, nullptr, eps, m->wte, m->logits, V, B, V, E, m->d_am_val,
                                m->d_am_idx, st, qh.wt, qh.q, qh.s));
-        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, qh.wt), B, m->d_next, st));
+        LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, qh.wt, B), B, m->d_next, st));
         if (advance)
             LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
         return MODEL_OK;
@@ -1546,7 +1546,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                     const QMat q = qmat(m, m->cfg.n_layer, 0);
                     CU(launch_dec_head(m->xb, E, nullptr, nullptr, 0.f, m->wte, m->logits, V,
                                        B, V, E, m->d_am_val, m->d_am_idx, st, q.wt, q.q, q.s));
-                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, q.wt), B, m->d_next,
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, dec_head_blocks(V, E, q.wt, B), B, m->d_next,
                                               st));
                     return MODEL_OK;
                 } else {
