@@ -211,8 +211,6 @@ def run_reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------- our arm --
-# fp32 decode steps of at most this many sequences run as one persistent kernel
-STEP_ROWS = 4
 
 
 def weight_bytes_per_elem(wl):
@@ -241,7 +239,7 @@ def roofline_of(m, wl, rows, measured, peaks):
         k[name]["share_ms"] = ms * per_step
         k[name]["work_per_launch"] = work
 
-    if steps > 0 and rows <= STEP_ROWS and wl.get("fmt", "f32") == "f32":
+    if steps > 0 and "decode_step" in measured:
         # the persistent step kernel: every weight matrix once, the KV cache of
         # every layer once, per step
         step_bytes = (12 * E * E * L + V * E) * 4 + L * rows * ctx * 2 * E * 4
@@ -379,9 +377,7 @@ def run_ours(args, rank, local_rank, world):
     # per-kernel live timings at this rank's shapes
     measured = {}
     ctx = T + n_new // 2
-    if n_new > 1 and size <= STEP_ROWS and fmt == "f32":
-        names = ["decode_step"]
-    elif n_new > 1:
+    if n_new > 1:
         names = ["decode_attention", "decode_qkv", "decode_fc", "decode_mlp_proj", "decode_head"]
     else:
         names = ["prefill_fc", "prefill_attention"]

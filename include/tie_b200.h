@@ -140,12 +140,13 @@ int model_weight_format(const model *m);
 const char *tie_last_device_error(void);
 
 /* ---- how small decode steps run ------------------------------------------
- * A decode step of at most 4 sequences (without attention statistics) runs as
- * ONE persistent kernel per step: TIE_STEP_PERSISTENT, the default. With
- * TIE_STEP_CHAINED it runs as the chain of per-layer kernels that batches of
- * 5..16 sequences use. Both form every sum in the same order, so they return
- * identical logits and tokens; the switch exists to compare and time them.
- * MODEL_ERR_ARG for any other value. */
+ * A decode step of at most 16 sequences runs as a chain of per-layer kernels
+ * linked by programmatic dependent launch: TIE_STEP_CHAINED, the default.
+ * With TIE_STEP_PERSISTENT a step of at most 4 sequences (fp32 weights,
+ * without attention statistics) runs as ONE persistent kernel instead. Both
+ * form every sum in the same order, so they return identical logits and
+ * tokens; the switch exists to compare and time them. MODEL_ERR_ARG for any
+ * other value. */
 enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1 };
 model_status model_set_step_kernel(model *m, int kind);
 

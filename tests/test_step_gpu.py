@@ -62,6 +62,7 @@ def test_step_long_context_bit_identical(n_seq):
 
 def test_step_launches_one_kernel_per_step():
     with _model("mini") as m:
+        m.set_step_kernel(tie_b200.TIE_STEP_PERSISTENT)
         prompts = synth.prompt_ids(m.vocab, 2, 9, seed=3)
         m.batch_reserve(2, 9 + 8)
         nxt, _ = m.prefill_batch(prompts)
@@ -94,3 +95,14 @@ def test_step_kind_validation():
     with _model("tiny") as m:
         with pytest.raises(tie_b200.ModelError):
             m.set_step_kernel(7)
+
+
+def test_chained_is_the_default():
+    """Batch-1 steps run the chained kernels unless the persistent one is asked for."""
+    with _model("mini") as m:
+        prompts = synth.prompt_ids(m.vocab, 1, 9, seed=4)
+        m.batch_reserve(1, 9 + 4)
+        nxt, _ = m.prefill_batch(prompts)
+        before = m.kernel_launches()
+        nxt, _ = m.decode_step_batch(nxt)
+        assert m.kernel_launches() - before > 1

@@ -478,6 +478,159 @@ attn_decode_fused_kernel(const float* __restrict__ qkv, const int32_t* __restric
 constexpr int PG = 16;   // positions per page and per chunk
 static_assert(PG == kPageRows, "a chunk is one page");
 
+// Small batches: a block of 8 warps per (sequence, head, 256 positions). Warp
+// w reduces chunks c0 + w and c0 + w + 8 of its range, both chunks' keys and
+// values loaded into registers before either is reduced, with the arithmetic
+// of attn_decode_fused_kernel<16>; the chunk partials go to shared memory.
+// When one block covers the whole context (<= 256 positions) it merges them
+// in chunk order itself (no global partials, no counters); otherwise the
+// partials go to global memory and the block completing a (sequence, head)'s
+// count merges all of them. Results are bit-identical to the fused kernel.
+constexpr int kSeqWarps = 8;
+constexpr int kSeqChunks = 2 * kSeqWarps;   // chunks per block
+
+struct ChunkRegs {
+    float4 k[8];
+    float2 v[PG];
+};
+
+__device__ __forceinline__ void chunk_load(ChunkRegs& r, const PagedKV& kv, int b, int h, int c, int n, int lane) {
+    const int pi = lane >> 1, half = lane & 1, E = kv.n_embd;
+    const size_t row0 = kv.row(b, c * PG);
+    if (pi < n) {
+        const float* kp = kv.k + (row0 + pi) * E + h * D;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r.k[j] = __ldcs(reinterpret_cast<const float4*>(kp + 4 * (2 * j + half)));
+    }
+    const float* vp = kv.v + row0 * E + h * D + 2 * lane;
+#pragma unroll
+    for (int i = 0; i < PG; ++i)
+        r.v[i] = i < n ? __ldcs(reinterpret_cast<const float2*>(vp + (size_t)i * E)) : make_float2(0.f, 0.f);
+}
+
+// chunk partial (max, sum, 64 weighted sums) of registers r into out
+__device__ __forceinline__ void chunk_reduce(const ChunkRegs& r, const float4 (&qv)[8], int n, float scale, int lane,
+                                             float* out) {
+    const int pi = lane >> 1;
+    float a = 0.f;
+    if (pi < n) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            a = fmaf(qv[j].x, r.k[j].x, a);
+            a = fmaf(qv[j].y, r.k[j].y, a);
+            a = fmaf(qv[j].z, r.k[j].z, a);
+            a = fmaf(qv[j].w, r.k[j].w, a);
+        }
+    }
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    const float sc = pi < n ? a * scale : -INFINITY;
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e = pi < n ? expf(sc - mx) : 0.f;
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < PG; ++i) {
+        const float ei = __shfl_sync(0xffffffffu, e, 2 * i);
+        if (i < n) l += ei;
+    }
+    float ox = 0.f, oy = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        const float e0 = __shfl_sync(0xffffffffu, e, 2 * g);
+        const float e1 = __shfl_sync(0xffffffffu, e, 2 * (g + 8));
+        float ax = 0.f, ay = 0.f;
+        if (g < n) {
+            ax = fmaf(e0, r.v[g].x, ax);
+            ay = fmaf(e0, r.v[g].y, ay);
+        }
+        if (g + 8 < n) {
+            ax = fmaf(e1, r.v[g + 8].x, ax);
+            ay = fmaf(e1, r.v[g + 8].y, ay);
+        }
+        if (g == 0) { ox = ax; oy = ay; }
+        else { ox += ax; oy += ay; }
+    }
+    *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(ox, oy);
+    if (lane == 0) *reinterpret_cast<float2*>(out) = make_float2(mx, l);
+}
+
+// merge of ns chunk partials P(k) (chunk order) by one warp: lane l writes
+// dims 2l, 2l + 1 of the head's output
+template <typename PF>
+__device__ __forceinline__ void merge_warp(const PF& P, int ns, int lane, float* out, float* out_hi, float* out_lo,
+                                           size_t oi) {
+    float m = -INFINITY;
+    for (int k = lane; k < ns; k += 32) m = fmaxf(m, P(k, 0));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float lt = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int k = 0; k < ns; ++k) {
+        const float cf = expf(P(k, 0) - m);
+        lt = fmaf(P(k, 1), cf, lt);
+        o0 = fmaf(P(k, 2 + 2 * lane), cf, o0);
+        o1 = fmaf(P(k, 3 + 2 * lane), cf, o1);
+    }
+    const float y0 = o0 / lt, y1 = o1 / lt;
+    if (out) *reinterpret_cast<float2*>(out + oi) = make_float2(y0, y1);
+    if (out_hi) {
+        const float h0 = tf32_hi(y0), h1 = tf32_hi(y1);
+        *reinterpret_cast<float2*>(out_hi + oi) = make_float2(h0, h1);
+        *reinterpret_cast<float2*>(out_lo + oi) = make_float2(__fsub_rn(y0, h0), __fsub_rn(y1, h1));
+    }
+}
+
+__global__ void __launch_bounds__(kSeqWarps * 32, 1)
+attn_decode_seq_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int H, PagedKV kv,
+                       int max_splits, float scale, float* __restrict__ part, int* __restrict__ counters,
+                       float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo) {
+    const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
+    __shared__ __align__(16) float s_part[kSeqChunks][PART + 2];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    const int ctx = lens[b] + 1, ns = (ctx + PG - 1) / PG;
+    const int nsp = (ns + kSeqChunks - 1) / kSeqChunks;
+    if (sp >= nsp) return;
+    const int c0 = sp * kSeqChunks, c1 = min(ns, c0 + kSeqChunks);
+    const int E = kv.n_embd;
+    float4 qv[8];
+    {
+        const float* q = qkv + (size_t)b * 3 * E + h * D;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qv[j] = *reinterpret_cast<const float4*>(q + 4 * (2 * j + (lane & 1)));
+    }
+    const int ca = c0 + warp, cb = c0 + warp + kSeqWarps;
+    ChunkRegs ra, rb;
+    if (ca < c1) chunk_load(ra, kv, b, h, ca, min(PG, ctx - ca * PG), lane);
+    if (cb < c1) chunk_load(rb, kv, b, h, cb, min(PG, ctx - cb * PG), lane);
+    if (ca < c1) chunk_reduce(ra, qv, min(PG, ctx - ca * PG), scale, lane, s_part[warp]);
+    if (cb < c1) chunk_reduce(rb, qv, min(PG, ctx - cb * PG), scale, lane, s_part[warp + kSeqWarps]);
+    __syncthreads();
+    const size_t oi = (size_t)b * H * D + h * D + 2 * lane;
+    if (nsp == 1) {
+        if (warp == 0)
+            merge_warp([&](int k, int f) { return s_part[k][f]; }, ns, lane, out, out_hi, out_lo, oi);
+        return;
+    }
+    // several blocks per (sequence, head): partials to global, the last merges
+    float* pbase = part + (size_t)(b * H + h) * max_splits * PART;
+    for (int i = threadIdx.x; i < (c1 - c0) * PART; i += kSeqWarps * 32)
+        pbase[(size_t)c0 * PART + i] = s_part[i / PART][i % PART];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&counters[b * H + h], 1) == nsp - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (warp == 0) {
+        merge_warp([&](int k, int f) { return __ldcg(pbase + (size_t)k * PART + f); }, ns, lane, out, out_hi, out_lo,
+                   oi);
+        if (lane == 0) counters[b * H + h] = 0;
+    }
+}
+
 // Large batches, persistent, one warp per unit: a unit is up to kUnitChunks
 // consecutive 16-position chunks of one (sequence, head). Units are numbered
 // (sequence, split, head), head fastest; each CTA takes a contiguous range of
@@ -802,6 +955,13 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
             const int grid = (int)std::min<long long>((units + kWarpsPerCta - 1) / kWarpsPerCta, 2LL * sms);
             e = launch_pdl(attn_decode_warp_kernel, dim3(grid), dim3(kWarpThreads), smem, st, qkv, lens, B, H, kv,
                            max_splits, scale, part, counters, out, out_hi, out_lo);
+            return e != cudaSuccess ? e : cudaGetLastError();
+        }
+        if (fine) {
+            // a block per (sequence, head, 256 positions)
+            const int nsp = (max_splits + kSeqChunks - 1) / kSeqChunks;
+            cudaError_t e = launch_pdl(attn_decode_seq_kernel, dim3(H, B, nsp), dim3(kSeqWarps * 32), 0, st, qkv,
+                                       lens, H, kv, max_splits, scale, part, counters, out, out_hi, out_lo);
             return e != cudaSuccess ? e : cudaGetLastError();
         }
         cudaError_t e = fine ? launch_pdl(attn_decode_fused_kernel<16>, dim3(splits, H, B), dim3(128), 0, st, qkv,

@@ -251,7 +251,7 @@ struct model {
     std::map<GraphKey, GraphEntry> graphs;
 
     // the persistent decode step (k_step.cu)
-    int step_kind = TIE_STEP_PERSISTENT;
+    int step_kind = TIE_STEP_CHAINED;
     StepLayer* d_step_layers = nullptr;
     unsigned* d_sync = nullptr;      // the step kernel's stage counters
     int step_state[5] = {0, 0, 0, 0, 0};  // per batch size: 0 unknown, 1 runs, -1 does not
@@ -636,10 +636,11 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
 }
 
 // Runs one decode step, from a graph when statistics are off.
-// Whether a step of B sequences takes the persistent kernel; allocates its
-// layer table and counters on first use.
-bool use_step(model* m, int B, const kv_cache* cache) {
-    if (m->step_kind != TIE_STEP_PERSISTENT || m->stats_on || m->wfmt != WF_F32 || B < 1 || B > 4) return false;
+// Whether the persistent kernel can run a step of B sequences (fp32 weights,
+// no attention statistics, a cache it can index); allocates its layer table
+// and counters on first use.
+bool step_applies(model* m, int B, const kv_cache* cache) {
+    if (m->stats_on || m->wfmt != WF_F32 || B < 1 || B > 4) return false;
     if (!cache || cache->pages_per_seq > step_max_pages()) return false;
     int& state = m->step_state[B];
     if (state == 0) {
@@ -673,6 +674,11 @@ bool use_step(model* m, int B, const kv_cache* cache) {
         m->d_step_layers = d;
     }
     return true;
+}
+
+// A step takes the persistent kernel when it applies and the model asks for it.
+bool use_step(model* m, int B, const kv_cache* cache) {
+    return m->step_kind == TIE_STEP_PERSISTENT && step_applies(m, B, cache);
 }
 
 // The whole decode step of B <= 4 sequences as one persistent kernel.
@@ -1429,7 +1435,7 @@ model_status model_step_trace(model* m, size_t rows, size_t context, uint64_t* o
     if (!m->pool || (int)rows > m->pool->n_seq || (int)context > m->pool->capacity) return MODEL_ERR_CAPACITY;
     model_status rc = ensure_slots(m, rows, m->pool->capacity);
     if (rc != MODEL_OK) return rc;
-    if (!use_step(m, (int)rows, m->pool)) return MODEL_ERR_ARG;
+    if (!step_applies(m, (int)rows, m->pool)) return MODEL_ERR_ARG;
     const size_t ev = (size_t)step_trace_events(m->cfg.n_layer), G = (size_t)m->step_grid;
     *per_cta = ev;
     *n_cta = G;
@@ -1564,7 +1570,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                               EPI_BIAS_GELU, nullptr, m->ff_hi, m->ff_lo, 4 * E);
             case TIE_KERNEL_DECODE_STEP:
                 // the step without advancing: every launch sees the same lengths
-                if (!use_step(m, B, m->pool)) return MODEL_ERR_ARG;
+                if (!step_applies(m, B, m->pool)) return MODEL_ERR_ARG;
                 return run_step(m, B, m->pool, false, nullptr, 0);
         }
         return MODEL_ERR_ARG;

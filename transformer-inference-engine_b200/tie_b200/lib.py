@@ -292,7 +292,7 @@ class Model:
         return library().model_weight_format(self.h)
 
     def set_step_kernel(self, kind):
-        """TIE_STEP_PERSISTENT (default) or TIE_STEP_CHAINED for decode steps of <= 4 sequences."""
+        """TIE_STEP_CHAINED (default) or TIE_STEP_PERSISTENT (decode steps of <= 4 sequences)."""
         _chk(library().model_set_step_kernel(self.h, kind), "model_set_step_kernel")
 
     def step_trace(self, rows: int, context: int) -> np.ndarray:
