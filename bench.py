@@ -213,6 +213,15 @@ def run_reference_arm(args, rank, world):
 # ------------------------------------------------------------- our arm --
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of a
+# roofline kernel, from one ncu capture of that kernel at exactly the shape the
+# workload times it at: (shape, kernel, rows, context) -> bytes
+NCU_TRAFFIC = {
+    ("small", "decode_attention", 256, 288): 453_929_216 + 9_000_448,
+    ("small", "decode_attention", 1, 192): 1_223_424 + 0,
+}
+
+
 def weight_bytes_per_elem(wl):
     return {"f32": 4, "bf16": 2, "int8": 1}[wl.get("fmt", "f32")]
 
@@ -265,8 +274,9 @@ def roofline_of(m, wl, rows, measured, peaks):
             4.0 * rows * E * T * (T + 1) / 2)
     dom = max(k, key=lambda n: k[n]["share_ms"])
     d = k[dom]
+    traffic = NCU_TRAFFIC.get((wl["shape"], dom, rows, ctx if steps > 0 else wl["n_prompt"]))
     roof = {"kernel": dom, "bound": d["bound"], "achieved": d["achieved"], "peak": d["peak"],
-            "unit": d["unit"], "frac": d["frac"], "traffic": None,
+            "unit": d["unit"], "frac": d["frac"], "traffic": traffic,
             "peak_source": "measured" if peaks else "fallback",
             "work_per_launch": d["work_per_launch"]}
     return roof, k
