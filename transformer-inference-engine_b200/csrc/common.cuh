@@ -198,6 +198,7 @@ cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float
 // position included), split over position chunks, then combined
 // (model.c:826-850).
 int attn_decode_max_splits(int capacity);
+int attn_decode_kernels(int B);
 // With `counters` (B * H ints, zero on first use; the kernel leaves them zero)
 // and no statistics, one fused kernel; else split + merge kernels. `err` is
 // set when a bounded wait of the large-batch kernel expires.

@@ -650,19 +650,15 @@ attn_decode_seq_kernel(const float* __restrict__ qkv, const int32_t* __restrict_
 // Each chunk is reduced with the arithmetic of attn_decode_fused_kernel<16>
 // -- lane 2 pi + half scores position pi over its half of the dims, then the
 // chunk max, the probabilities summed in position order, and the weighted
-// values as eight position groups added in group order -- and merged with its
-// formula, so results are bit-identical to the small-batch path. A unit's chunk partials are counted in with one acquire-release
-// atomic per (sequence, head); the warp completing the count merges.
+// values as eight position groups added in group order -- and its partial
+// (max, sum, 64 weighted sums) is written to `part`. The loop carries no
+// counters or merges: attn_decode_merge_kernel, chained after it with
+// programmatic dependent launch, merges every (sequence, head) with the fused
+// kernel's formula, so results are bit-identical to the small-batch path.
 constexpr int kUnitChunks = 4;
 constexpr int kWarpThreads = 256;
 constexpr int kWarpsPerCta = kWarpThreads / 32;
 constexpr int kWarpMaxSeqs = 8192;
-
-__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
 
 __device__ __forceinline__ float4 ld_stream4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
 __device__ __forceinline__ float2 ld_stream2(const float* p) { return __ldcs(reinterpret_cast<const float2*>(p)); }
@@ -707,8 +703,7 @@ struct ChunkCursor {
 
 __global__ void __launch_bounds__(kWarpThreads, 2)
 attn_decode_warp_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int B, int H, PagedKV kv,
-                        int max_splits, float scale, float* __restrict__ part, int* __restrict__ counters,
-                        float* __restrict__ out, float* __restrict__ out_hi, float* __restrict__ out_lo) {
+                        int max_splits, float scale, float* __restrict__ part) {
     extern __shared__ int s_seq[];
     int* s_start = s_seq;           // [B + 1] unit offsets
     int* s_ctx = s_seq + B + 1;     // [B] contexts
@@ -777,7 +772,6 @@ attn_decode_warp_kernel(const float* __restrict__ qkv, const int32_t* __restrict
         if (nx_new && lane < D / 4) qn = *reinterpret_cast<const float4*>(q_ptr(nx) + 4 * lane);
     }
     __syncwarp();
-    int run_n = 0;
     while (true) {
         const int n = cc.rows();
         const bool more = nx.u < end;
@@ -836,51 +830,7 @@ attn_decode_warp_kernel(const float* __restrict__ qkv, const int32_t* __restrict
         float* pp = pbase + (size_t)cc.c * PART;
         *reinterpret_cast<float2*>(pp + 2 + 2 * lane) = make_float2(ox, oy);
         if (lane == 0) *reinterpret_cast<float2*>(pp) = make_float2(mx, l);
-        ++run_n;
 
-        if (cc.c + 1 == cc.c1) {
-            // the unit is done: count its chunks in; the warp completing the count merges
-            const int ns = (cc.ctx + PG - 1) / PG;
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atom_add_acq_rel(&counters[cc.b * H + cc.h], run_n) + run_n == ns;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            run_n = 0;
-            if (last) {
-                __syncwarp();   // lane 0 acquired the other warps' partials for the whole warp
-                float m = -INFINITY;
-                for (int k = lane; k < ns; k += 32) m = fmaxf(m, __ldcg(pbase + (size_t)k * PART));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                float lt = 0.f, o0 = 0.f, o1 = 0.f;
-                for (int k0 = 0; k0 < ns; k0 += 4) {
-                    float2 ml[4], ov[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        if (k0 + k < ns) {
-                            ml[k] = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + k) * PART));
-                            ov[k] = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + k) * PART + 2 + 2 * lane));
-                        }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        if (k0 + k < ns) {
-                            const float cf = expf(ml[k].x - m);
-                            lt = fmaf(ml[k].y, cf, lt);
-                            o0 = fmaf(ov[k].x, cf, o0);
-                            o1 = fmaf(ov[k].y, cf, o1);
-                        }
-                }
-                const float y0 = o0 / lt, y1 = o1 / lt;
-                const size_t oi = (size_t)cc.b * H * D + cc.h * D + 2 * lane;
-                if (out) *reinterpret_cast<float2*>(out + oi) = make_float2(y0, y1);
-                if (out_hi) {
-                    const float h0 = tf32_hi(y0), h1 = tf32_hi(y1);
-                    *reinterpret_cast<float2*>(out_hi + oi) = make_float2(h0, h1);
-                    *reinterpret_cast<float2*>(out_lo + oi) = make_float2(__fsub_rn(y0, h0), __fsub_rn(y1, h1));
-                }
-                if (lane == 0) counters[cc.b * H + cc.h] = 0;
-            }
-        }
         if (!more) break;
         // advance: the next chunk becomes current
         if (nx_new) {
@@ -897,7 +847,67 @@ attn_decode_warp_kernel(const float* __restrict__ qkv, const int32_t* __restrict
     }
 }
 
+// One warp per (sequence, head): its chunk partials from `part` merged in
+// chunk order with the formula of attn_decode_fused_kernel<16> (lane l: dims
+// 2l and 2l + 1); the chunk maxima and sums are read by lane k for chunk k and
+// shuffled, each lane's weighted sums eight chunks at a time.
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
+attn_decode_merge_kernel(const int32_t* __restrict__ lens, int B, int H, int max_splits,
+                         const float* __restrict__ part, float* __restrict__ out, float* __restrict__ out_hi,
+                         float* __restrict__ out_lo) {
+    pdl_trigger();
+    pdl_wait();
+    const int gw = blockIdx.x * kMergeWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= B * H) return;
+    const int b = gw / H, h = gw - b * H;
+    const int ns = (lens[b] + PG) / PG;   // chunks of context lens[b] + 1
+    const float* pbase = part + (size_t)gw * max_splits * PART;
+    float m = -INFINITY;
+    for (int k = lane; k < ns; k += 32) m = fmaxf(m, __ldcg(pbase + (size_t)k * PART));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float lt = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int k0 = 0; k0 < ns; k0 += 32) {
+        float2 ml = make_float2(0.f, 0.f);
+        if (k0 + lane < ns) ml = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + lane) * PART));
+        const int kn = min(32, ns - k0);
+        for (int k1 = 0; k1 < kn; k1 += 8) {
+            float2 ov[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k1 + k < kn)
+                    ov[k] = __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(k0 + k1 + k) * PART + 2 + 2 * lane));
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float mk = __shfl_sync(0xffffffffu, ml.x, (k1 + k) & 31);
+                const float lk = __shfl_sync(0xffffffffu, ml.y, (k1 + k) & 31);
+                if (k1 + k < kn) {
+                    const float cf = expf(mk - m);
+                    lt = fmaf(lk, cf, lt);
+                    o0 = fmaf(ov[k].x, cf, o0);
+                    o1 = fmaf(ov[k].y, cf, o1);
+                }
+            }
+        }
+    }
+    const float y0 = o0 / lt, y1 = o1 / lt;
+    const size_t oi = (size_t)b * H * D + h * D + 2 * lane;
+    if (out) *reinterpret_cast<float2*>(out + oi) = make_float2(y0, y1);
+    if (out_hi) {
+        const float h0 = tf32_hi(y0), h1 = tf32_hi(y1);
+        *reinterpret_cast<float2*>(out_hi + oi) = make_float2(h0, h1);
+        *reinterpret_cast<float2*>(out_lo + oi) = make_float2(__fsub_rn(y0, h0), __fsub_rn(y1, h1));
+    }
+}
+
 }  // namespace
+
+// Kernels one launch_attn_decode issues with counters and without statistics:
+// the streaming kernel and its merge for batches above 16 (up to the
+// sequences it indexes), else one.
+int attn_decode_kernels(int B) { return B > 16 && B <= kWarpMaxSeqs ? 2 : 1; }
 
 // Partial-buffer sizing: the finest chunking any launch uses (16 positions).
 int attn_decode_max_splits(int capacity) { return (capacity + 15) / 16; }
@@ -954,7 +964,10 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
             const long long units = (long long)B * H * ((max_splits + kUnitChunks - 1) / kUnitChunks);
             const int grid = (int)std::min<long long>((units + kWarpsPerCta - 1) / kWarpsPerCta, 2LL * sms);
             e = launch_pdl(attn_decode_warp_kernel, dim3(grid), dim3(kWarpThreads), smem, st, qkv, lens, B, H, kv,
-                           max_splits, scale, part, counters, out, out_hi, out_lo);
+                           max_splits, scale, part);
+            if (e != cudaSuccess) return e;
+            e = launch_pdl(attn_decode_merge_kernel, dim3((B * H + kMergeWarps - 1) / kMergeWarps),
+                           dim3(kMergeWarps * 32), 0, st, lens, B, H, max_splits, part, out, out_hi, out_lo);
             return e != cudaSuccess ? e : cudaGetLastError();
         }
         if (fine) {

@@ -406,7 +406,6 @@ model_status matmul(model* m, bool decode, int rows, Mat x, int ldx, Mat w, int 
     const int out = y_hi ? (y ? TC_OUT_F32_HILO : TC_OUT_HILO) : TC_OUT_F32;
     const int splits = decode ? tc_splits_for(N, K) : 1;
     LAUNCH(launch_tc_gemm(op, a, epi, out, splits, st));
-    if (splits > 1) ++m->launches;  // the split reduction
     return MODEL_OK;
 }
 
@@ -586,7 +585,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
                                    EPI_QKV_KV, &view, m->d_lens, st, q0.wt, q0.q, q0.s));
             LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, m->attn, stats, st,
                                       nullptr, nullptr, m->d_attn_cnt, m->d_err));
-            if (stats) ++m->launches;  // the separate merge kernel
+            m->launches += (stats ? 2 : attn_decode_kernels(B)) - 1;  // a separate merge kernel
             LAUNCH(launch_dec_gemv(m->attn, E, nullptr, nullptr, eps, w.proj_w, w.proj_b, m->x, E, B, E, E,
                                    EPI_BIAS_RESID, nullptr, nullptr, st, q1.wt, q1.q, q1.s));
             LAUNCH(launch_layernorm(m->x, w.ln2_w, w.ln2_b, m->xb, B, E, eps, st));
@@ -614,7 +613,7 @@ model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t*
         LAUNCH(launch_kv_store_decode(m->qkv, m->d_lens, B, view, st));
         LAUNCH(launch_attn_decode(m->qkv, m->d_lens, B, H, view, max_splits, m->d_part, nullptr, stats, st,
                                   m->attn_hi, m->attn_lo, m->d_attn_cnt, m->d_err));
-        if (stats) ++m->launches;  // the separate merge kernel
+        m->launches += (stats ? 2 : attn_decode_kernels(B)) - 1;  // a separate merge kernel
         if ((rc = matmul(m, true, B, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
                          EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
             return rc;
