@@ -698,14 +698,16 @@ bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
 
 // Split count for a decode-sized matmul, chosen from N and K only, so that a
 // row's result never depends on how many rows are in the batch: the largest
-// power of two up to a portable cluster (8) with N tiles x splits <= 74, so
-// that two 128-row tiles (the largest decode batch) make one wave of CTAs,
-// and at least four 16-wide k-blocks per split.
+// power of two up to a portable cluster (8) with N tiles x splits <= 96 --
+// two 128-row tiles (the largest decode batch) then make at most 192 CTAs,
+// which one wave holds at two CTAs per SM (71 clusters of 4 or 33 of 8 are
+// resident at this kernel's shared memory) -- and at least four 16-wide
+// k-blocks per split.
 int tc_splits_for(int N, int K) {
     const int n_tiles = (N + 127) / 128;
     const int kb = K / BK;
     int s = 1;
-    while (s < 8 && n_tiles * s * 2 <= 74 && s * 2 <= kb / 4) s *= 2;
+    while (s < 8 && n_tiles * s * 2 <= 96 && s * 2 <= kb / 4) s *= 2;
     return s;
 }
 
