@@ -363,6 +363,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
 // first stages are requested before griddepcontrol.wait, the activation (A)
 // tiles and every read of a previous kernel's output after it.
 constexpr int kSplitStages = 3;
+constexpr int kMaxSplits = 16;   // CTAs of a cluster (16 is a non-portable size)
 constexpr int kRedLd = 128 + 4;   // staging row stride in floats: conflict-free float4 stores down a column
 static_assert((size_t)kSplitStages * (2u * BM * 64 + 2u * 128 * 64) >= (size_t)BM * kRedLd * sizeof(float),
               "the partial overlays the drained ring");
@@ -544,13 +545,13 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
         if (row >= p.M || col >= p.N) continue;
         const uint32_t local = smem_u32(red + (size_t)r * kRedLd + 4 * c4);
         // every split's value in flight at once, then summed in split order
-        float4 v[8];
+        float4 v[kMaxSplits];
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
+        for (int s = 0; s < kMaxSplits; ++s)
             if (s < splits) v[s] = ld_cluster4(mapa_cluster(local, (uint32_t)s));
         float4 acc = v[0];
 #pragma unroll
-        for (int s = 1; s < 8; ++s)
+        for (int s = 1; s < kMaxSplits; ++s)
             if (s < splits) {
                 acc.x = __fadd_rn(acc.x, v[s].x);
                 acc.y = __fadd_rn(acc.y, v[s].y);
@@ -648,7 +649,7 @@ cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStr
     return cudaGetLastError();
 }
 
-// Decode shapes: one cluster of `splits` CTAs per 128 x 128 tile (splits <= 8),
+// Decode shapes: one cluster of `splits` CTAs per 128 x 128 tile (splits <= 16),
 // programmatic dependent launch.
 template <int EPI, int OUT>
 cudaError_t launch_split(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
@@ -660,6 +661,10 @@ cudaError_t launch_split(const TcOperands& op, TcArgs a, int splits, cudaStream_
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_split_kernel<EPI, OUT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    if (splits > 8) {
+        e = cudaFuncSetAttribute(tc_gemm_split_kernel<EPI, OUT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
     a.kb_per_split = (a.K / BK + splits - 1) / splits;
     const int used = (a.K / BK + a.kb_per_split - 1) / a.kb_per_split;
     a.splits = used;
@@ -698,7 +703,7 @@ bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
 
 // Split count for a decode-sized matmul, chosen from N and K only, so that a
 // row's result never depends on how many rows are in the batch: the largest
-// power of two up to a portable cluster (8) with N tiles x splits <= 96 --
+// power of two up to a portable cluster (8; 16 below) with N tiles x splits <= 96 --
 // two 128-row tiles (the largest decode batch) then make at most 192 CTAs,
 // which one wave holds at two CTAs per SM (71 clusters of 4 or 33 of 8 are
 // resident at this kernel's shared memory) -- and at least four 16-wide
@@ -708,6 +713,10 @@ int tc_splits_for(int N, int K) {
     const int kb = K / BK;
     int s = 1;
     while (s < 8 && n_tiles * s * 2 <= 96 && s * 2 <= kb / 4) s *= 2;
+    // narrow matrices with long rows (N <= 768, K >= 3072: the MLP
+    // down-projection) take a 16-CTA cluster (non-portable; 14 are resident,
+    // two 128-row tiles of N <= 768 need at most 12)
+    if (s == 8 && n_tiles * 2 <= 12 && 16 <= kb / 8) s = 16;
     return s;
 }
 
