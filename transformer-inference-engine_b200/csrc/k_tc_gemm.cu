@@ -141,17 +141,33 @@ constexpr size_t smem_bytes() {
     return 1024 /* alignment slack */ + (size_t)stages<BN>() * stage_bytes<BN>() + 256 /* barriers */;
 }
 
+// The persistent kernel's tile is MT x 128 rows by BN columns: A (hi and lo)
+// MT x 128 rows, B BN rows per 16-wide k-block.
+template <int BN, int MT>
+constexpr uint32_t stage_bytes_mt() { return 2u * MT * BM * 64 + 2u * BN * 64; }
+
+template <int BN, int MT>
+constexpr int stages_mt() { return (int)((192u * 1024) / stage_bytes_mt<BN, MT>()); }
+
+template <int BN, int MT>
+constexpr size_t smem_bytes_mt() {
+    return 1024 /* alignment slack */ + (size_t)stages_mt<BN, MT>() * stage_bytes_mt<BN, MT>() + 256 /* barriers */;
+}
+
 // Persistent, warp-specialised: each block loops over output tiles
-// (blockIdx.x, + gridDim.x, ...). The TMEM accumulator is double-buffered, so
-// the epilogue warps drain tile i while the MMA warp accumulates tile i + 1.
-template <int BN, int EPI, int OUT>
+// (blockIdx.x, + gridDim.x, ...) of MT x 128 rows by BN columns; with MT = 2
+// each B tile feeds two accumulators (the two 128-row halves), so B crosses
+// from memory once per 256 rows. The TMEM accumulators are double-buffered,
+// so the epilogue warps drain tile i while the MMA warp accumulates tile i + 1.
+template <int BN, int MT, int EPI, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                TcArgs p) {
-    constexpr int S = stages<BN>();
-    constexpr uint32_t kStage = stage_bytes<BN>();
-    constexpr uint32_t kTileA = BM * 64, kTileB = BN * 64;
+    constexpr int S = stages_mt<BN, MT>();
+    constexpr uint32_t kStage = stage_bytes_mt<BN, MT>();
+    constexpr uint32_t kTileA = MT * BM * 64, kTileB = BN * 64;
+    constexpr uint32_t kAcc = MT * BN;   // TMEM columns of one accumulator buffer
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage);
@@ -163,7 +179,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_n = (p.N + BN - 1) / BN, tiles_m = (p.M + BM - 1) / BM;
+    const int tiles_n = (p.N + BN - 1) / BN, tiles_m = (p.M + MT * BM - 1) / (MT * BM);
     const int tiles_mn = tiles_n * tiles_m;
     const int n_tiles = tiles_mn * p.splits;
     const int kb_total = p.K / BK;
@@ -182,7 +198,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)(2 * BN)));
+                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)(2 * kAcc)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -216,7 +232,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
             bool ok = true;
             for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
                 const int z = t / tiles_mn, r = t % tiles_mn;
-                const int m0 = (r / tiles_n) * BM, n0 = (r % tiles_n) * BN;
+                const int m0 = (r / tiles_n) * MT * BM, n0 = (r % tiles_n) * BN;
                 int kb0, nkb;
                 tile_k_range(z, kb0, nkb);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
@@ -251,7 +267,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                 const uint32_t use = (uint32_t)(i >> 1);
                 if (!wait(smem_u32(&tempty[buf]), (use & 1u) ^ 1u)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t acc = tmem + (uint32_t)(buf * BN);
+                const uint32_t acc = tmem + (uint32_t)(buf * kAcc);
                 int kb0, nkb;
                 tile_k_range(t / tiles_mn, kb0, nkb);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
@@ -261,13 +277,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                     const uint32_t base = smem_u32(smem + s * kStage);
 #pragma unroll
                     for (int j = 0; j < BK / 8; ++j) {  // k-steps of 8 tf32 (32 bytes)
-                        const uint64_t a_hi = sw64_desc(base + j * 32);
-                        const uint64_t a_lo = sw64_desc(base + kTileA + j * 32);
                         const uint64_t b_hi = sw64_desc(base + 2 * kTileA + j * 32);
                         const uint64_t b_lo = sw64_desc(base + 2 * kTileA + kTileB + j * 32);
-                        mma_tf32(acc, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-                        mma_tf32(acc, a_hi, b_lo, idesc, 1u);
-                        mma_tf32(acc, a_hi, b_hi, idesc, 1u);
+#pragma unroll
+                        for (int mh = 0; mh < MT; ++mh) {   // 128-row halves: rows 128 mh.. of the A tiles
+                            const uint64_t a_hi = sw64_desc(base + mh * BM * 64 + j * 32);
+                            const uint64_t a_lo = sw64_desc(base + kTileA + mh * BM * 64 + j * 32);
+                            const uint32_t d = acc + (uint32_t)(mh * BN);
+                            mma_tf32(d, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                            mma_tf32(d, a_hi, b_lo, idesc, 1u);
+                            mma_tf32(d, a_hi, b_hi, idesc, 1u);
+                        }
                     }
                     mma_commit(smem_u32(&empty[s]));
                 }
@@ -282,15 +302,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int buf = i & 1;
             const uint32_t use = (uint32_t)(i >> 1);
-            const int z = t / tiles_mn, r = t % tiles_mn;
-            const int m0 = (r / tiles_n) * BM, n0 = (r % tiles_n) * BN;
+            const int r = t % tiles_mn;
+            const int n0 = (r % tiles_n) * BN;
             const bool ok = wait(smem_u32(&tfull[buf]), use & 1u);
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int cc = 0; cc < MT * (BN / 32); ++cc) {
+                const int mh = cc / (BN / 32), c = cc % (BN / 32);
+                const int row = (r / tiles_n) * MT * BM + mh * BM + q * 32 + lane;
                 uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), v);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAcc + mh * BN + c * 32), v);
                 if (!ok || row >= p.M) continue;
                 const int col0 = n0 + c * 32;
                 const bool full_chunk = col0 + 32 <= p.N;
@@ -341,7 +362,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * kAcc)));
     }
 }
 
@@ -632,20 +653,20 @@ int num_sms() {
     return n;
 }
 
-template <int BN, int EPI, int OUT>
+template <int BN, int MT, int EPI, int OUT>
 cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStream_t st) {
     CUtensorMap m[4];
-    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, BM) || !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, BM) ||
+    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, MT * BM) || !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, MT * BM) ||
         !make_map(&m[2], op.b_hi, a.N, a.K, op.ldb, BN) || !make_map(&m[3], op.b_lo, a.N, a.K, op.ldb, BN))
         return cudaErrorInvalidValue;
-    constexpr size_t smem = smem_bytes<BN>();
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, OUT>,
+    constexpr size_t smem = smem_bytes_mt<BN, MT>();
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, MT, EPI, OUT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM) * splits;
+    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + MT * BM - 1) / (MT * BM)) * splits;
     TcArgs b = a;
     b.splits = splits;
-    tc_gemm_kernel<BN, EPI, OUT><<<std::min(tiles, num_sms()), THREADS, smem, st>>>(m[0], m[1], m[2], m[3], b);
+    tc_gemm_kernel<BN, MT, EPI, OUT><<<std::min(tiles, num_sms()), THREADS, smem, st>>>(m[0], m[1], m[2], m[3], b);
     return cudaGetLastError();
 }
 
@@ -690,7 +711,12 @@ template <int EPI, int OUT>
 cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
     if (splits <= 1) {
         a.kb_per_split = a.K / BK;
-        return launch_bn<128, EPI, OUT>(op, a, 1, st);
+        // 129-256 rows (decode batches, the tied head): 256-row tiles, so each
+        // B tile crosses from memory once (measured on B200: head over 256
+        // rows 250 -> 216-235 us; a prefill FC of 8192 rows slows 300 -> 315
+        // us with them, so larger matmuls keep 128-row tiles)
+        if (a.M > BM && a.M <= 2 * BM) return launch_bn<128, 2, EPI, OUT>(op, a, 1, st);
+        return launch_bn<128, 1, EPI, OUT>(op, a, 1, st);
     }
     return launch_split<EPI, OUT>(op, a, splits, st);
 }
