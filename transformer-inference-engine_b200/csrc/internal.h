@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/kv_cache.h"
+#include "../../include/safetensors.h"
 #include "common.cuh"
 
 // The cache: per layer a key pool and a value pool of `rows` fp32 rows of
@@ -47,5 +48,8 @@ cudaError_t copy_any(void* dst, const void* src, size_t bytes);
 
 cudaError_t launch_gemm_nn(const float* A, int lda, const float* B, int ldb, float* C, int ldc,
                            int M, int N, int K, cudaStream_t st);
+
+// Bytes [offset, offset + n) of tensor t's data (safetensors.cpp).
+st_status st_tensor_read_range(const st_file* f, const st_tensor* t, uint64_t offset, void* dst, size_t n);
 
 }  // namespace tie

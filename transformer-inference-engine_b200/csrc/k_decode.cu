@@ -28,6 +28,7 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kMaxRows = 16;
+constexpr int kFreeSms = 16;   // SMs a GEMV's grid leaves to the next kernel
 
 __device__ __forceinline__ float4 ld_stream(const float* p) {
     float4 v;
@@ -302,7 +303,11 @@ int resident_blocks() {
             per_sm = 1;
         }
     }
-    return per_sm * sm_count();
+    // all but kFreeSms SMs: the blocks of the next kernel in the chain (a
+    // LayerNorm row, the attention heads) become resident under programmatic
+    // dependent launch while this one runs (measured on B200: GPT-2 medium,
+    // batch 8, 4086 -> 4213 tok/s; batch 1 unchanged within 1%)
+    return per_sm * (sm_count() - kFreeSms);
 }
 
 template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>

@@ -790,17 +790,6 @@ model_status check_tensor(st_file* f, const std::string& inv, const char* name, 
     return MODEL_OK;
 }
 
-model_status load_tensor(model* m, st_file* f, const std::string& inv, const char* name, int nd,
-                         long long d0, long long d1, std::vector<float>* host, InvEntry* out) {
-    (void)m;
-    const st_tensor* t = nullptr;
-    model_status rc = check_tensor(f, inv, name, nd, d0, d1, out, &t);
-    if (rc != MODEL_OK) return rc;
-    try { host->resize((size_t)(t->nbytes / sizeof(float))); } catch (...) { return MODEL_ERR_NOMEM; }
-    if (st_tensor_read(f, t, host->data(), t->nbytes) != ST_OK) return MODEL_ERR_WEIGHTS;
-    return MODEL_OK;
-}
-
 // Every tensor the forward pass uses, checked before any device work so that a
 // bad artifact is refused without touching the GPU.
 model_status check_all(st_file* f, const std::string& inv, const model_config& c) {
@@ -855,8 +844,13 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
     m->cproj = cproj;
     model_status rc = MODEL_OK;
     st_file* f = nullptr;
-    std::vector<float> host, tmp_host;
     float* staging = nullptr;
+    // pinned staging: file chunks are read into one buffer while the other's
+    // copy to the device runs
+    constexpr size_t kPinBytes = 32u << 20;
+    void* pin[2] = {nullptr, nullptr};
+    cudaEvent_t pin_done[2] = {nullptr, nullptr};
+    int pin_cur = 0;
     const char* c = cfg_text.c_str();
     double eps = 0.0;
     model_config& cf = m->cfg;
@@ -915,55 +909,64 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
             rc = MODEL_ERR_NOMEM;
             goto fail;
         }
+        for (int i = 0; i < 2; ++i) {
+            if (cudaHostAlloc(&pin[i], kPinBytes, cudaHostAllocDefault) != cudaSuccess ||
+                cudaEventCreateWithFlags(&pin_done[i], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                rc = MODEL_ERR_NOMEM;
+                goto fail;
+            }
+        }
         float* cursor = m->d_weights;
         auto take = [&](size_t n) { float* p = cursor; cursor += n; return p; };
-        // uploads `host` (d0 x d1 row-major) to dst, transposed to d1 x d0 when asked
-        auto upload = [&](float* dst, size_t d0, size_t d1, bool transpose) -> model_status {
-            if (!transpose) {
-                CU(cudaMemcpy(dst, host.data(), d0 * d1 * sizeof(float), cudaMemcpyHostToDevice));
-            } else {
-                CU(cudaMemcpy(staging, host.data(), d0 * d1 * sizeof(float), cudaMemcpyHostToDevice));
-                CU(launch_transpose(staging, dst, (int)d0, (int)d1, nullptr));
-                CU(cudaDeviceSynchronize());
+        // tensor `name` (d0 x d1 row-major in the file) to dst on the device,
+        // transposed to d1 x d0 when asked: chunks through the pinned buffers,
+        // asynchronous copies on the model's stream
+        auto fetch = [&](const char* name, int nd, size_t d0, size_t d1, InvEntry* out, float* dst,
+                         bool transpose) -> model_status {
+            const st_tensor* t = nullptr;
+            model_status r = check_tensor(f, inv, name, nd, (long long)d0, (long long)d1, out, &t);
+            if (r != MODEL_OK) return r;
+            char* target = reinterpret_cast<char*>(transpose ? staging : dst);
+            for (uint64_t off = 0; off < t->nbytes; off += kPinBytes) {
+                const size_t n = (size_t)std::min<uint64_t>(kPinBytes, t->nbytes - off);
+                CU(cudaEventSynchronize(pin_done[pin_cur]));
+                if (st_tensor_read_range(f, t, off, pin[pin_cur], n) != ST_OK) return MODEL_ERR_WEIGHTS;
+                CU(cudaMemcpyAsync(target + off, pin[pin_cur], n, cudaMemcpyHostToDevice, m->st));
+                CU(cudaEventRecord(pin_done[pin_cur], m->st));
+                pin_cur ^= 1;
             }
+            if (transpose) CU(launch_transpose(staging, dst, (int)d0, (int)d1, m->st));
             return MODEL_OK;
         };
         InvEntry e;
 #define TRY(x) do { rc = (x); if (rc != MODEL_OK) goto fail; } while (0)
-        TRY(load_tensor(m, f, inv, "wte.weight", 2, cf.vocab_size, cf.n_embd, &host, &e));
         m->wte = take(V * E);
-        TRY(upload(m->wte, V, E, false));
+        TRY(fetch("wte.weight", 2, V, E, &e, m->wte, false));
         record(m, "wte.weight", e, 0, "rows are tokens: the lookup table and, as stored, the tied head");
-        TRY(load_tensor(m, f, inv, "wpe.weight", 2, cf.n_ctx, cf.n_embd, &host, &e));
         m->wpe = take((size_t)cf.n_ctx * E);
-        TRY(upload(m->wpe, cf.n_ctx, E, false));
+        TRY(fetch("wpe.weight", 2, (size_t)cf.n_ctx, E, &e, m->wpe, false));
         record(m, "wpe.weight", e, 0, "rows are positions: learned absolute, as stored");
-        TRY(load_tensor(m, f, inv, "ln_f.weight", 1, cf.n_embd, 0, &host, &e));
         m->lnf_w = take(E);
-        TRY(upload(m->lnf_w, 1, E, false));
-        TRY(load_tensor(m, f, inv, "ln_f.bias", 1, cf.n_embd, 0, &host, &e));
+        TRY(fetch("ln_f.weight", 1, E, 0, &e, m->lnf_w, false));
         m->lnf_b = take(E);
-        TRY(upload(m->lnf_b, 1, E, false));
+        TRY(fetch("ln_f.bias", 1, E, 0, &e, m->lnf_b, false));
         m->layers.resize(L);
         for (int l = 0; l < cf.n_layer; ++l) {
             Layer& y = m->layers[l];
             char name[64];
             auto vec = [&](const char* fmt, size_t n, float** dst) -> model_status {
                 std::snprintf(name, sizeof name, fmt, l);
-                model_status r = load_tensor(m, f, inv, name, 1, (long long)n, 0, &host, nullptr);
-                if (r != MODEL_OK) return r;
                 *dst = take(n);
-                return upload(*dst, 1, n, false);
+                return fetch(name, 1, n, 0, nullptr, *dst, false);
             };
             // A matrix stored [in, out] in the file becomes [out, in] (K-major) on the
             // device: the layout of every matmul kernel here.
             auto mat = [&](const char* fmt, size_t din, size_t dout, bool stored_in_out,
                            float** dst) -> model_status {
                 std::snprintf(name, sizeof name, fmt, l);
-                model_status r = load_tensor(m, f, inv, name, 2, (long long)din, (long long)dout, &host, &e);
-                if (r != MODEL_OK) return r;
                 *dst = take(din * dout);
-                return upload(*dst, din, dout, stored_in_out);
+                return fetch(name, 2, din, dout, &e, *dst, stored_in_out);
             };
             TRY(vec("h.%d.ln_1.weight", E, &y.ln1_w));
             TRY(vec("h.%d.ln_1.bias", E, &y.ln1_b));
@@ -990,6 +993,8 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
                                "[input, output] as stored; held [output, input] on the device");
             TRY(vec("h.%d.mlp.c_proj.bias", E, &y.mlp_b));
         }
+        // every copy and transpose on the model's stream has landed
+        CU(cudaStreamSynchronize(m->st));
         // tf32 splits of every matrix, for the tensor-core matmul
         {
             const size_t mats = V * E + L * (3 * E * E + E * E + 4 * E * E + 4 * E * E);
@@ -1025,11 +1030,20 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
 #undef TRY
     }
     cudaFree(staging);
+    for (int i = 0; i < 2; ++i) {
+        if (pin_done[i]) cudaEventDestroy(pin_done[i]);
+        if (pin[i]) cudaFreeHost(pin[i]);
+    }
     st_close(f);
     *out = m;
     return MODEL_OK;
 fail:
+    if (m && m->st) cudaStreamSynchronize(m->st);   // no copy still reads a pinned buffer
     cudaFree(staging);
+    for (int i = 0; i < 2; ++i) {
+        if (pin_done[i]) cudaEventDestroy(pin_done[i]);
+        if (pin[i]) cudaFreeHost(pin[i]);
+    }
     if (f) st_close(f);
     model_free(m);
     return rc;
@@ -1214,7 +1228,7 @@ model_status model_prefill(model* m, const int32_t* ids, size_t T, float* logits
     if ((rc = stats_begin(m)) != MODEL_OK) return rc;
     if ((rc = copy_ids_to_device(m, ids, T)) != MODEL_OK) return rc;
     if ((rc = run_prefill(m, 1, (int)T, use_cache ? m->kv : nullptr, 0)) != MODEL_OK) return rc;
-    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    const int V = m->cfg.vocab_size;
     // the tied head at every position (model.c:778-780)
     if ((rc = prefill_head(m, (int)T, 0, 1)) != MODEL_OK) return rc;
     CU(cudaMemcpyAsync(logits, m->logits, T * (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
@@ -1278,7 +1292,7 @@ model_status model_decode_step(model* m, const int32_t* ids, size_t T, float* lo
     if ((rc = stats_begin(m)) != MODEL_OK) return rc;
     if ((rc = copy_ids_to_device(m, ids, T)) != MODEL_OK) return rc;
     if ((rc = run_prefill(m, 1, (int)T, nullptr, 0)) != MODEL_OK) return rc;
-    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    const int V = m->cfg.vocab_size;
     // the head at the last position only, with prefill's kernel (model.c:913-916)
     if ((rc = prefill_head(m, 1, T - 1, 1)) != MODEL_OK) return rc;
     CU(cudaMemcpyAsync(logits, m->logits, (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, m->st));
@@ -1314,7 +1328,7 @@ model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
 
 static model_status batch_prefill_impl(model* m, size_t n_seq, size_t T, float* logits_host,
                                        int32_t* next_host, bool host_ids, const int32_t* ids) {
-    const int E = m->cfg.n_embd, V = m->cfg.vocab_size;
+    const int V = m->cfg.vocab_size;
     model_status rc;
     if (host_ids) {
         if ((rc = copy_ids_to_device(m, ids, n_seq * T)) != MODEL_OK) return rc;

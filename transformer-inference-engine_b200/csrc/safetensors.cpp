@@ -282,3 +282,17 @@ const char* st_metadata(const st_file* f, const char* key) {
 int st_has_metadata(const st_file* f) { return f ? f->has_metadata : 0; }
 
 }  // extern "C"
+
+namespace tie {
+
+// Bytes [offset, offset + n) of tensor t's data into dst (the loader streams a
+// tensor through pinned staging buffers this way).
+st_status st_tensor_read_range(const st_file* f, const st_tensor* t, uint64_t offset, void* dst, size_t n) {
+    if (!f || !t || (!dst && n)) return ST_ERR_ARG;
+    if (offset > t->nbytes || n > t->nbytes - offset) return ST_ERR_ARG;
+    if (fseeko(f->fp, (off_t)(t->file_offset + offset), SEEK_SET) != 0) return ST_ERR_READ;
+    if (n && std::fread(dst, 1, n, f->fp) != n) return ST_ERR_READ;
+    return ST_OK;
+}
+
+}  // namespace tie
