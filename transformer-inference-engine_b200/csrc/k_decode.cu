@@ -32,7 +32,10 @@ constexpr int kFreeSms = 16;   // SMs a GEMV's grid leaves to the next kernel
 
 __device__ __forceinline__ float4 ld_stream(const float* p) {
     float4 v;
-    asm("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+    // volatile: the compiler keeps the load where it is written, ahead of
+    // griddepcontrol.wait; a plain asm without memory operands may be moved
+    // past the wait, putting the whole weight round trip after it
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
         : "l"(p));
     return v;
@@ -128,10 +131,36 @@ dec_gemv_kernel(DecArgs a) {
             }
     };
 
+    // The epilogue's operands. A thread finishes at most one (row, activation
+    // row) pair of a group: pair q = lane of the slice-0 warp, row q / M and
+    // activation row q % M. Its bias and int8 scale are weights, loaded with
+    // the group's weights before the dependency wait; its residual and
+    // sequence length are read right after the wait (or after the previous
+    // group's epilogue), so no load is left between the sums and the store.
+    static_assert(EPI == DEC_HEAD || RPW * MB <= 32, "one epilogue pair per thread");
+    const bool ep_on = EPI != DEC_HEAD && warp % WS == 0 && lane < RPW * a.M;
+    const int ep_r = ep_on ? lane / a.M : 0, ep_m = ep_on ? lane % a.M : 0;
+    float ep_bias = 0.f, ep_scale = 1.f, ep_res = 0.f;
+    int ep_len = 0;
+    auto ep_weights = [&](int row0, float& b, float& sc) {
+        if (ep_on && row0 + ep_r < a.N) {
+            b = __ldg(a.bias + row0 + ep_r);
+            if constexpr (WT == 2) sc = __ldg(a.scale + row0 + ep_r);
+        }
+    };
+    auto ep_inputs = [&](int row0) {
+        if (ep_on && row0 + ep_r < a.N) {
+            if constexpr (EPI == DEC_BIAS_RESID) ep_res = a.y[(size_t)ep_m * a.ldy + row0 + ep_r];
+            if constexpr (EPI == DEC_QKV_KV) ep_len = a.lens[ep_m];
+        }
+    };
+
     // 1. the first group's weights, before the dependency wait
     load((blockIdx.x * GROUPS + grp) * RPW);
+    ep_weights((blockIdx.x * GROUPS + grp) * RPW, ep_bias, ep_scale);
     pdl_trigger();
     pdl_wait();
+    ep_inputs((blockIdx.x * GROUPS + grp) * RPW);
 
     const float* X = a.x;
     const int ldx = a.ldx;
@@ -200,7 +229,13 @@ dec_gemv_kernel(DecArgs a) {
             }
         }
         // the next group's weights go out while this group is finished
-        if ((blk + gridDim.x) * RPB < n_iter_rows) load(((blk + gridDim.x) * GROUPS + grp) * RPW);
+        const bool more = (blk + gridDim.x) * RPB < n_iter_rows;
+        const int next0 = ((blk + gridDim.x) * GROUPS + grp) * RPW;
+        float nbias = 0.f, nscale = 1.f;
+        if (more) {
+            load(next0);
+            ep_weights(next0, nbias, nscale);
+        }
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
@@ -222,29 +257,24 @@ dec_gemv_kernel(DecArgs a) {
         // 4. epilogue: slice sums in slice order; thread t of a row group
         //    handles (row r, activation row m) pairs
         if constexpr (EPI != DEC_HEAD) {
-            const int t = threadIdx.x % (WS * 32);
-            if (warp % WS == 0 || WS == 1) {
-                for (int q = (WS == 1 ? lane : t); q < RPW * a.M; q += (WS == 1 ? 32 : WS * 32)) {
-                    const int r = q / a.M, m = q % a.M;
-                    const int j = row0 + r;
-                    if (j >= a.N) continue;
-                    float sum = s_part[grp][0][r][m];
+            const int j = row0 + ep_r;
+            if (ep_on && j < a.N) {
+                const int r = ep_r, m = ep_m;
+                float sum = s_part[grp][0][r][m];
 #pragma unroll
-                    for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
-                    if constexpr (WT == 2) sum = sum * __ldg(a.scale + j);
-                    float* yp = a.y + (size_t)m * a.ldy + j;
-                    float v;
-                    if constexpr (EPI == DEC_BIAS || EPI == DEC_QKV_KV) v = apply_epi<EPI_BIAS>(sum, a.bias, j, yp);
-                    else if constexpr (EPI == DEC_BIAS_GELU) v = apply_epi<EPI_BIAS_GELU>(sum, a.bias, j, yp);
-                    else v = apply_epi<EPI_BIAS_RESID>(sum, a.bias, j, yp);
-                    *yp = v;
-                    if constexpr (EPI == DEC_QKV_KV) {
-                        const int E = a.kv.n_embd;
-                        if (j >= E) {
-                            const size_t row = a.kv.row(m, a.lens[m]);
-                            if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
-                            else a.kv.v[row * E + (j - 2 * E)] = v;
-                        }
+                for (int k = 1; k < WS; ++k) sum += s_part[grp][k][r][m];
+                if constexpr (WT == 2) sum = sum * ep_scale;
+                // bias, GELU or residual as apply_epi (common.cuh) computes them
+                float v = __fadd_rn(sum, ep_bias);
+                if constexpr (EPI == DEC_BIAS_GELU) v = gelu_new_ref(v);
+                if constexpr (EPI == DEC_BIAS_RESID) v = __fadd_rn(ep_res, v);
+                a.y[(size_t)m * a.ldy + j] = v;
+                if constexpr (EPI == DEC_QKV_KV) {
+                    const int E = a.kv.n_embd;
+                    if (j >= E) {
+                        const size_t row = a.kv.row(m, ep_len);
+                        if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
+                        else a.kv.v[row * E + (j - 2 * E)] = v;
                     }
                 }
             }
@@ -266,6 +296,11 @@ dec_gemv_kernel(DecArgs a) {
                         else if (v == v && beats(v, j, bv, bi)) { bv = v; bi = j; }
                     }
             }
+        }
+        if (more) {
+            ep_bias = nbias;
+            ep_scale = nscale;
+            ep_inputs(next0);
         }
         __syncthreads();   // s_part is rewritten by the next group
     }
