@@ -99,8 +99,14 @@ __device__ __forceinline__ float chunk_elem(const float4& c, int e) {
 // weights are loaded before the dependency wait; each later group's are
 // loaded while the previous group's sums are finished. MB is the row bucket:
 // a.M <= MB activation rows.
+// At one activation row the matrices need up to 768 blocks (GPT-2 small's FC
+// and MLP): seven resident blocks per SM (at most 72 registers) keep them in
+// one wave; the fp32 and bf16 variants of up to 8 chunks fit without spills.
+template <int EPI, int MB, int CPL, int WT>
+constexpr int dec_min_blocks() { return EPI != DEC_HEAD && MB == 1 && CPL <= 8 && WT != 2 ? 7 : 1; }
+
 template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, dec_min_blocks<EPI, MB, CPL, WT>())
 dec_gemv_kernel(DecArgs a) {
     constexpr int GROUPS = kWarps / WS;          // row groups per block
     constexpr int RPB = GROUPS * RPW;            // rows per block iteration
