@@ -225,10 +225,41 @@ __global__ void argmax_rows_kernel(const float* __restrict__ L, int ldl, int N, 
     const float* r = L + (size_t)(row_offset + (size_t)b * row_stride) * ldl;
     float bv = 0.f;
     int bi = -1;
-    for (int i = threadIdx.x; i < N; i += blockDim.x) {
-        const float v = r[i];
+    auto take = [&](float v, int i) {
         if (v == v && beats(v, i, bv, bi)) { bv = v; bi = i; }
+    };
+    // The winner is the maximum of a total order (value, then lower index),
+    // so the scan may visit the row in any order. Rows start anywhere (the
+    // row length is the vocabulary), so up to three scalars lead to a 16-byte
+    // boundary; the body goes in float4s, kArgU of them in flight per thread.
+    constexpr int kArgU = 4;
+    const int head = min(N, (int)((16u - ((uint32_t)(uintptr_t)r & 15u)) & 15u) / 4);
+    if ((int)threadIdx.x < head) take(r[threadIdx.x], threadIdx.x);
+    const float4* r4 = reinterpret_cast<const float4*>(r + head);
+    const int n4 = (N - head) >> 2, T = blockDim.x;
+    int c = threadIdx.x;
+    for (; c + (kArgU - 1) * T < n4; c += kArgU * T) {
+        float4 v[kArgU];
+#pragma unroll
+        for (int u = 0; u < kArgU; ++u) v[u] = __ldg(r4 + c + u * T);
+#pragma unroll
+        for (int u = 0; u < kArgU; ++u) {
+            const int i = head + 4 * (c + u * T);
+            take(v[u].x, i);
+            take(v[u].y, i + 1);
+            take(v[u].z, i + 2);
+            take(v[u].w, i + 3);
+        }
     }
+    for (; c < n4; c += T) {
+        const float4 v = __ldg(r4 + c);
+        const int i = head + 4 * c;
+        take(v.x, i);
+        take(v.y, i + 1);
+        take(v.z, i + 2);
+        take(v.w, i + 3);
+    }
+    for (int i = head + 4 * n4 + threadIdx.x; i < N; i += T) take(r[i], i);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
