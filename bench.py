@@ -258,11 +258,11 @@ def roofline_of(m, wl, rows, measured, peaks):
         add("decode_attention", measured.get("decode_attention"), L * steps, "hbm", kv_bytes)
         for name, N, K in (("decode_qkv", 3 * E, E), ("decode_fc", 4 * E, E), ("decode_mlp_proj", E, 4 * E)):
             ms = measured.get(name)
-            if rows <= 16:
+            if rows <= 8:   # the streaming GEMVs (model.cu kGemvRows)
                 add(name, ms, L * steps, "hbm", N * K * weight_bytes_per_elem(wl) + rows * (N + K) * 4)
             else:
                 add(name, ms, L * steps, "tensor", 2.0 * rows * N * K)
-        if rows <= 16:
+        if rows <= 8:
             add("decode_head", measured.get("decode_head"), steps, "hbm",
                 V * E * weight_bytes_per_elem(wl) + rows * V * 4)
         else:

@@ -125,7 +125,7 @@ model_status model_time_kernel(model *m, int kernel, size_t rows, size_t context
  * The formats apply to the five matrix kinds -- qkv, attention proj, fc, mlp
  * proj, and the tied wte (head and embedding lookup alike); LayerNorm, biases
  * and wpe stay fp32. Accumulation is fp32 throughout. Decode steps of at most
- * 16 sequences stream the compact copies (2 or 1 byte per element); every other
+ * 8 sequences stream the compact copies (2 or 1 byte per element); every other
  * path computes with the fp32 values the copies stand for, so the model is the
  * same model whichever kernels run. A format's copies are built on the device
  * on first selection and kept. */
@@ -140,7 +140,7 @@ int model_weight_format(const model *m);
 const char *tie_last_device_error(void);
 
 /* ---- how small decode steps run ------------------------------------------
- * A decode step of at most 16 sequences runs as a chain of per-layer kernels
+ * A decode step of at most 8 sequences runs as a chain of per-layer kernels
  * linked by programmatic dependent launch: TIE_STEP_CHAINED, the default.
  * With TIE_STEP_PERSISTENT a step of at most 4 sequences (fp32 weights,
  * without attention statistics) runs as ONE persistent kernel instead. Both

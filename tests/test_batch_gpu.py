@@ -26,7 +26,7 @@ def m(mini_paths):
     mod.close()
 
 
-@pytest.mark.parametrize("B", [8, 40])  # the GEMV path (<= 16 rows) and the tiled path
+@pytest.mark.parametrize("B", [8, 40])  # the GEMV path (<= 8 rows) and the tiled path
 def test_batch_invariance(m, B):
     prompts = synth.prompt_ids(m.vocab, B, 20, seed=31)
     n_new = 24
@@ -70,7 +70,7 @@ def test_small_batches_match_single_sequence_api(m):
 def test_shards_reproduce_the_full_batch(m, world):
     """What `bench.py --gpus N` does on N GPUs, replayed shard by shard on one:
     every shard's tokens equal the full batch's rows."""
-    n = 160  # every shard keeps more than 16 sequences: the same matmul path as the full batch
+    n = 160  # every shard keeps more than 16 sequences: the same matmul and attention path as the full batch
     prompts = synth.prompt_ids(m.vocab, n, 16, seed=51)
     m.batch_reserve(n, 16 + 10)
     full = m.generate_greedy(prompts, 10)

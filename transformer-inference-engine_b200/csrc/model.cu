@@ -165,8 +165,14 @@ struct Mat {
     const float* lo;
 };
 
-// Decode batches of at most this many rows take the streaming GEMV.
-constexpr int kGemvRows = 16;
+// Decode batches of at most this many rows take the streaming GEMV; larger
+// ones the tensor-core matmuls. Measured on B200 (GPT-2 small, each matmul
+// alone): at 8 rows the two paths are level (QKV 10.1 vs 10.6 us, FC 9.7 vs
+// 13.1, MLP 16.9 vs 13.3, head 87 vs 101), at 12-16 rows the GEMV is behind
+// (QKV 14.9, FC 14.6, MLP 22.2, head 152 us at 16 rows), and a whole greedy
+// step of 16 sequences took 1.21 ms on the GEMVs against 0.93 ms for 17 on
+// the tensor cores.
+constexpr int kGemvRows = 8;
 
 // One instantiated decode graph per (batch size, cache, advance, output) key,
 // with the number of kernels one replay runs.
