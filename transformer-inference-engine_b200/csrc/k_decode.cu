@@ -102,8 +102,12 @@ __device__ __forceinline__ float chunk_elem(const float4& c, int e) {
 // At one activation row the matrices need up to 768 blocks (GPT-2 small's FC
 // and MLP): seven resident blocks per SM (at most 72 registers) keep them in
 // one wave; the fp32 and bf16 variants of up to 8 chunks fit without spills.
+// Every other variant gives 0, which leaves the minimum unspecified: an
+// explicit 1 is not neutral, ptxas then spends registers freely (the 8-row
+// MLP variant went from 166 to 214 registers, 3 to 2 blocks per SM, and
+// GPT-2 medium at batch 8 lost a fifth of its throughput).
 template <int EPI, int MB, int CPL, int WT>
-constexpr int dec_min_blocks() { return EPI != DEC_HEAD && MB == 1 && CPL <= 8 && WT != 2 ? 7 : 1; }
+constexpr int dec_min_blocks() { return EPI != DEC_HEAD && MB == 1 && CPL <= 8 && WT != 2 ? 7 : 0; }
 
 template <int EPI, int MB, int RPW, int WS, int CPL, int WT = 0>
 __global__ void __launch_bounds__(kWarps * 32, dec_min_blocks<EPI, MB, CPL, WT>())
