@@ -1,4 +1,5 @@
-// k_decode.cu -- the small-batch decode matmuls (at most 16 sequences),
+// k_decode.cu -- the small-batch decode matmuls (up to 16 rows; the decode step
+// sends batches of at most 8 sequences here, larger ones to the tensor cores),
 // chained with programmatic dependent launch.
 //
 // A decode step at batch 1 moves ~0.5 GB of fp32 weights through a few dozen
