@@ -30,11 +30,12 @@ REF_INVENTORY_BIN = os.path.join(HERE, "_ref", "st_inventory")
 
 def build(reference_root: str | None = None) -> None:
     """Compiles liboracle.so, and the reference binaries when the reference
-    source tree is present."""
+    source tree is present (its location: `reference_root`, else the
+    TIE_REFERENCE_ROOT environment variable, else the Makefile's default)."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
-    ref = reference_root or os.environ.get("TIE_REFERENCE_ROOT", "/root/reference")
-    if os.path.isfile(os.path.join(ref, "src", "model.c")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
+    ref = reference_root or os.environ.get("TIE_REFERENCE_ROOT")
+    cmd = ["make", "-s", "-C", HERE, "ref-if-present"] + ([f"REF={ref}"] if ref else [])
+    subprocess.run(cmd, check=True)
 
 
 def reference_available() -> bool:
@@ -173,6 +174,11 @@ class Oracle:
         if rc:
             raise RuntimeError(f"orc_decode_nocache rc={rc}")
         return out
+
+    def kv_set_length(self, n: int) -> None:
+        rc = _load().orc_kv_set_length(self._h, int(n))
+        if rc:
+            raise RuntimeError(f"orc_kv_set_length rc={rc}")
 
     def greedy(self, prompt, n_new: int):
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -14,6 +14,16 @@
  * usage: ref_gpt2 WEIGHTS INVENTORY CONFIG IDS.bin N_SEQ N_PROMPT N_NEW OUT.bin
  *                 [--first-seq S] [--cproj transposed] [--prefill-logits all|last|none]
  *                 [--step-logits] [--nocache] [--topk K] [--prefill-topk]
+ *                 [--time-contexts C1,C2,... [--rounds R]]
+ *
+ * With --time-contexts the driver measures instead of generating: for the
+ * first sequence it times model_prefill over the whole prompt (the cache is
+ * written), then, R times over, one model_decode_step_cached at each listed
+ * context C (the cache length set to C - 1 with model_kv_set_length, the ids
+ * past the prompt filled with the prefill's greedy token). Decode cost is
+ * affine in the context, so these samples give the cost of every step of a
+ * generation ("none" times the prefill alone). Nothing is written to OUT.bin;
+ * stdout gets one JSON line.
  *
  * IDS.bin holds N_SEQ x N_PROMPT int32 ids (row-major); sequences
  * [first-seq, first-seq + N_SEQ) of it are run. OUT.bin receives, per sequence:
@@ -75,6 +85,8 @@ int main(int argc, char **argv)
     size_t first = 0;
     int transposed = 0, step_logits = 0, nocache = 0, K = 2, prefill_topk = 0;
     const char *pl = "none";
+    const char *time_ctx = NULL;
+    int rounds = 1;
     for (int i = 9; i < argc; ++i) {
         if (!strcmp(argv[i], "--first-seq") && i + 1 < argc) first = (size_t)atol(argv[++i]);
         else if (!strcmp(argv[i], "--cproj") && i + 1 < argc) transposed = !strcmp(argv[++i], "transposed");
@@ -83,6 +95,8 @@ int main(int argc, char **argv)
         else if (!strcmp(argv[i], "--nocache")) nocache = 1;
         else if (!strcmp(argv[i], "--topk") && i + 1 < argc) K = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--prefill-topk")) prefill_topk = 1;
+        else if (!strcmp(argv[i], "--time-contexts") && i + 1 < argc) time_ctx = argv[++i];
+        else if (!strcmp(argv[i], "--rounds") && i + 1 < argc) rounds = atoi(argv[++i]);
         else { fprintf(stderr, "unknown flag %s\n", argv[i]); return 2; }
     }
     if (K < 1 || K > 64) { fprintf(stderr, "--topk must be in [1, 64]\n"); return 2; }
@@ -131,6 +145,49 @@ int main(int argc, char **argv)
         (step_logits && !steps)) {
         fprintf(stderr, "allocation or output open failed\n");
         return 1;
+    }
+
+    if (time_ctx) {
+        fclose(fo);
+        int ctx[64], n_ctx = 0;
+        for (const char *c = time_ctx; strcmp(time_ctx, "none") != 0 && *c && n_ctx < 64;) {
+            ctx[n_ctx++] = atoi(c);
+            const char *comma = strchr(c, ',');
+            if (!comma) break;
+            c = comma + 1;
+        }
+        for (int i = 0; i < n_ctx; ++i)
+            if (ctx[i] <= (int)n_prompt || (size_t)ctx[i] > total - 1 || rounds < 1) {
+                fprintf(stderr, "--time-contexts: each context must be in (n_prompt, n_prompt + n_new - 1]\n");
+                return 2;
+            }
+        memcpy(ids, all_ids + first * n_prompt, n_prompt * sizeof(int32_t));
+        double a = now_ms();
+        rc = model_prefill(m, ids, n_prompt, plog, n_prompt * V);
+        const double prefill_ms = now_ms() - a;
+        if (rc != MODEL_OK) { fprintf(stderr, "prefill: %s\n", model_strerror(rc)); return 1; }
+        const int32_t fill = model_argmax(plog + (n_prompt - 1) * V, V);
+        for (size_t t = n_prompt; t < total; ++t) ids[t] = fill;
+        printf("{\"load_ms\": %.3f, \"mode\": \"sampled\", \"n_prompt\": %zu, \"prefill_ms\": %.3f, "
+               "\"contexts\": [", load_ms, n_prompt, prefill_ms);
+        for (int i = 0; i < n_ctx; ++i) printf("%s%d", i ? ", " : "", ctx[i]);
+        printf("], \"rounds\": [");
+        for (int r = 0; r < rounds; ++r) {
+            printf("%s[", r ? ", " : "");
+            for (int i = 0; i < n_ctx; ++i) {
+                if (model_kv_set_length(m, ctx[i] - 1) != MODEL_OK) { fprintf(stderr, "kv_set_length\n"); return 1; }
+                a = now_ms();
+                rc = model_decode_step_cached(m, ids, (size_t)ctx[i], one, V);
+                const double ms = now_ms() - a;
+                if (rc != MODEL_OK) { fprintf(stderr, "decode at %d: %s\n", ctx[i], model_strerror(rc)); return 1; }
+                printf("%s%.3f", i ? ", " : "", ms);
+            }
+            printf("]");
+            fflush(stdout);
+        }
+        printf("]}\n");
+        model_free(m);
+        return 0;
     }
 
     printf("{\"load_ms\": %.3f, \"n_seq\": %zu, \"n_prompt\": %zu, \"n_new\": %zu, \"seqs\": [",

@@ -57,7 +57,44 @@ def prompts_for(name: str) -> np.ndarray:
     return synth.prompt_ids(V, s["n_seq"], s["n_prompt"], s["prompt_seed"])
 
 
-def make(name: str, workers: int, n_seq_limit: int | None = None) -> None:
+def _save(name: str, s: dict, prompts: np.ndarray, results: list, t0: float, extra: dict) -> None:
+    n_seq = len(results)
+    out = {"prompts": prompts[:n_seq],
+           "ids": np.stack([r[0]["ids"] for r in results]),
+           "topk_ids": np.stack([r[0]["topk_ids"] for r in results]),
+           "topk_vals": np.stack([r[0]["topk_vals"] for r in results])}
+    for key in ("prefill_topk_ids", "prefill_topk_vals", "prefill_logits", "step_logits"):
+        if key in results[0][0]:
+            out[key] = np.stack([r[0][key] for r in results])
+    out.update(extra)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    meta = dict(spec=s, n_seq_recorded=n_seq, seconds=round(time.time() - t0, 1),
+                cpu_timing=[r[1] for r in results],
+                producer="oracle/_ref/ref_gpt2 (reference src/model.c, kv_cache.c, gemm_naive.c, "
+                         "safetensors.c compiled unmodified with -O3 -mavx2 -mfma -std=gnu11 "
+                         "-ffp-contract=off)")
+    with open(os.path.join(HERE, f"{name}.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+
+
+def _load_existing(name: str):
+    """The sequences an earlier run recorded, as (seq dict, timing) pairs."""
+    npz, meta = os.path.join(HERE, f"{name}.npz"), os.path.join(HERE, f"{name}.json")
+    if not (os.path.isfile(npz) and os.path.isfile(meta)):
+        return []
+    g = np.load(npz)
+    with open(meta) as f:
+        timing = json.load(f)["cpu_timing"]
+    keys = [k for k in ("ids", "topk_ids", "topk_vals", "prefill_topk_ids", "prefill_topk_vals",
+                        "prefill_logits", "step_logits") if k in g.files]
+    return [({k: g[k][i] for k in keys}, timing[i]) for i in range(g["ids"].shape[0])]
+
+
+def make(name: str, workers: int, n_seq_limit: int | None = None, resume: bool = False) -> None:
+    """Runs the reference on every sequence of fixture `name`.  With `resume`,
+    the sequences already in the fixture are kept and only the rest are run;
+    the fixture is rewritten after every chunk of sequences, so an interrupted
+    run loses at most one chunk."""
     s = spec(name)
     w, inv, cfg = synth.ensure_model(s["shape"], seed=s["weight_seed"], ln_affine=s["ln_affine"])
     prompts = prompts_for(name)
@@ -70,37 +107,39 @@ def make(name: str, workers: int, n_seq_limit: int | None = None) -> None:
         seqs, timing = oracle.run_reference(w, inv, cfg, prompts, s["n_new"], first_seq=i, n_seq=1, **kw)
         return seqs[0], timing["seqs"][0]
 
-    with ThreadPoolExecutor(max_workers=workers) as ex:
-        results = list(ex.map(one, range(n_seq)))
-    out = {"prompts": prompts[:n_seq],
-           "ids": np.stack([r[0]["ids"] for r in results]),
-           "topk_ids": np.stack([r[0]["topk_ids"] for r in results]),
-           "topk_vals": np.stack([r[0]["topk_vals"] for r in results])}
-    for key in ("prefill_topk_ids", "prefill_topk_vals", "prefill_logits", "step_logits"):
-        if key in results[0][0]:
-            out[key] = np.stack([r[0][key] for r in results])
+    results = _load_existing(name) if resume else []
+    if resume and results:
+        recorded = np.load(os.path.join(HERE, f"{name}.npz"))["prompts"]
+        if not np.array_equal(recorded, prompts[:len(results)]):
+            raise SystemExit(f"{name}: the recorded prompts differ from the fixture's seed; not resuming")
+    extra = {}
     if name == "tiny":
         t_seqs, _ = oracle.run_reference(w, inv, cfg, prompts, s["n_new"], n_seq=1, first_seq=0,
                                          prefill_logits="all", cproj_transposed=True, topk=s["topk"])
-        out["transposed_prefill_logits"] = t_seqs[0]["prefill_logits"][None]
-        out["transposed_ids"] = t_seqs[0]["ids"][None]
+        extra["transposed_prefill_logits"] = t_seqs[0]["prefill_logits"][None]
+        extra["transposed_ids"] = t_seqs[0]["ids"][None]
         torch_logits = torch_oracle(w, inv, cfg, prompts[0])
         if torch_logits is not None:
-            out["torch_prefill_logits"] = torch_logits[None]
-    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
-    meta = dict(spec=s, n_seq_recorded=n_seq, seconds=round(time.time() - t0, 1),
-                cpu_timing=[r[1] for r in results],
-                producer="oracle/_ref/ref_gpt2 (reference src/model.c, kv_cache.c, gemm_naive.c, "
-                         "safetensors.c compiled unmodified with -O3 -mavx2 -mfma -std=gnu11 "
-                         "-ffp-contract=off)")
-    with open(os.path.join(HERE, f"{name}.json"), "w") as f:
-        json.dump(meta, f, indent=1)
+            extra["torch_prefill_logits"] = torch_logits[None]
+    chunk = max(1, workers) * 2
+    with ThreadPoolExecutor(max_workers=workers) as ex:
+        while len(results) < n_seq:
+            lo = len(results)
+            hi = min(n_seq, lo + chunk)
+            results += list(ex.map(one, range(lo, hi)))
+            _save(name, s, prompts, results, t0, extra)
+            print(f"{name}: {len(results)}/{n_seq} sequences, {time.time() - t0:.1f} s", flush=True)
+    if not results:
+        return
+    _save(name, s, prompts, results, t0, extra)
     print(f"{name}: {n_seq} sequences in {time.time() - t0:.1f} s", flush=True)
 
 
 def torch_oracle(w, inv, cfg, ids):
     """The reference's PyTorch oracle on the same weights, if importable here."""
-    ref_dir = os.environ.get("TIE_REFERENCE_ROOT", "/root/reference")
+    ref_dir = os.environ.get("TIE_REFERENCE_ROOT")
+    if not ref_dir:
+        return None
     path = os.path.join(ref_dir, "reference")
     if not os.path.isfile(os.path.join(path, "reference_impl.py")):
         return None
@@ -118,11 +157,13 @@ def main(argv=None):
     p.add_argument("names", nargs="+", choices=sorted(FIXTURES))
     p.add_argument("--workers", type=int, default=max(1, (os.cpu_count() or 2) - 2))
     p.add_argument("--n-seq", type=int, default=None, help="record only the first N sequences")
+    p.add_argument("--resume", action="store_true",
+                   help="keep the sequences already recorded and run only the rest")
     a = p.parse_args(argv)
     if not oracle.reference_available():
         oracle.build()
     for n in a.names:
-        make(n, a.workers, a.n_seq)
+        make(n, a.workers, a.n_seq, a.resume)
 
 
 if __name__ == "__main__":

@@ -160,6 +160,20 @@ def test_load_refusals_before_device(tiny_paths, tmp_path):
     assert with_cfg(n_head=3) == S("MODEL_ERR_CONFIG")            # 128 % 3 != 0
     assert with_cfg(n_head=4, n_embd=128) in (S("MODEL_ERR_CONFIG"), S("MODEL_ERR_INVENTORY"))
     assert with_cfg(n_layer=3) == S("MODEL_ERR_INVENTORY")       # inventory says 2
+    # a real GPT-2 config carries booleans, nulls, floats and nested objects
+    # beside the fields the loader reads; an unreadable or truncated text is refused
+    raw = open(cfg).read()
+    try:
+        full = dict(base, scale_attn_weights=True, n_inner=None, resid_pdrop=0.1,
+                    task_specific_params={"text-generation": {"do_sample": True, "max_length": 50}})
+        json.dump(full, open(cfg, "w"), indent=2)
+        assert load(w, inv, cfg) in (S("MODEL_OK"), S("MODEL_ERR_DEVICE"))
+        open(cfg, "w").write(raw[: len(raw) // 2])
+        assert load(w, inv, cfg) == S("MODEL_ERR_CONFIG")
+        open(cfg, "w").write(raw.replace('"n_embd": 128', '"n_embd": "128"'))
+        assert load(w, inv, cfg) == S("MODEL_ERR_CONFIG")
+    finally:
+        open(cfg, "w").write(raw)
 
     text = open(inv).read()
 
@@ -172,6 +186,7 @@ def test_load_refusals_before_device(tiny_paths, tmp_path):
 
     assert with_inv(text.replace('{"name": "h.1.ln_2.bias",', '{"name": "h.1.ln_2.biax",')) == \
         S("MODEL_ERR_INVENTORY")
+    assert with_inv(text[: len(text) - 40]) == S("MODEL_ERR_INVENTORY")     # truncated
     line = [l for l in text.splitlines() if '"name": "h.0.mlp.c_fc.bias"' in l][0]
     assert with_inv(text.replace(line, line.replace('"F32"', '"F16"'))) == S("MODEL_ERR_DTYPE")
     assert with_inv(text.replace(line, line.replace('"shape": [512]', '"shape": [511]'))) == \

@@ -6,10 +6,11 @@ allocations outside its own allocator, a latency-bound loop that cannot take
 cudaMalloc's implicit synchronisation. This entry point keeps its scratch (the
 per-block partial maxima) in a fixed array inside the library instead.
 
-It is checked here, through the C ABI, against the existing entry points for the
-same computation: the tiled matmul of gemm_impl_sm100a for the logits (within
-the fp32 summation bound the kernel tests use) and model_argmax over those
-logits for the greedy ids, on two calls in a row that reuse the shared scratch.
+It is checked here, through the C ABI, on two calls in a row that reuse the
+shared scratch: the logits against the float64 product x . w^T (within the fp32
+summation bound the kernel tests use) and against the existing tiled matmul
+entry point of gemm_impl_sm100a, the greedy ids against model_argmax over its
+own logits, and a call without logits against the ids of the call with them.
 This file is collected last so a failure here comes after every other test.
 """
 import ctypes as C
@@ -44,13 +45,18 @@ def test_noalloc_head_matches_existing_entry_points():
         assert _call(L, x, w, rows, V, K, logits, nxt, stream) == 0
         torch.cuda.synchronize()
         got_logits, got_next = logits.cpu().numpy(), nxt.cpu().numpy()
-        ref_logits = tie_b200.gemm_tiled_bt(x_h, w_h)          # existing entry point
+        exact = x_h.astype(np.float64) @ w_h.astype(np.float64).T
         scale = np.abs(x_h).astype(np.float64) @ np.abs(w_h).astype(np.float64).T
+        assert np.all(np.abs(got_logits - exact) <= K * 6e-8 * scale), call
+        ref_logits = tie_b200.gemm_tiled_bt(x_h, w_h)          # existing entry point
         assert np.all(np.abs(got_logits - ref_logits) <= 2 * K * 6e-8 * scale), call
-        ref_next = np.array([tie_b200.argmax(r) for r in ref_logits], np.int32)
-        assert np.array_equal(got_next, ref_next), (call, got_next, ref_next)
         own = np.array([tie_b200.argmax(r) for r in got_logits], np.int32)
-        assert np.array_equal(got_next, own)
+        assert np.array_equal(got_next, own), (call, got_next, own)
+        # the same rows without a logits buffer: the same greedy ids
+        nxt2 = torch.full((rows,), -7, dtype=torch.int32, device="cuda")
+        assert _call(L, x, w, rows, V, K, None, nxt2, stream) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(nxt2.cpu().numpy(), got_next), call
 
 
 def test_noalloc_head_refuses_sizes_beyond_its_scratch():

@@ -171,6 +171,9 @@ cudaError_t launch_gemv(const float* X, int ldx, const float* W, int ldw, const 
                         float* Y, int ldy, int M, int N, int K, int epi, cudaStream_t st);
 // Head GEMV with fused argmax: logits[M,V] (optional) and per-block partial
 // maxima; finalize writes next[M] (lowest index on ties, NaN never wins).
+// Vocabulary rows one block of the greedy-head GEMV (launch_gemv_argmax) covers;
+// its launch has gemv_argmax_blocks(N) blocks, one partial maximum per (block, row).
+constexpr int kGemvArgmaxRowsPerBlock = 16;
 int gemv_argmax_blocks(int N);
 cudaError_t launch_gemv_argmax(const float* X, int ldx, const float* W, int ldw, float* logits,
                                int ldl, int M, int N, int K, float* part_val, int* part_idx,

@@ -21,6 +21,7 @@
 struct kv_cache {
     int n_layer = 0, n_embd = 0, capacity = 0, length = 0;
     int n_seq = 1, pages_per_seq = 0;
+    bool contiguous = true;   // kv_cache_create's one-sequence layout (whole-layer views exist)
     size_t rows = 0;    // physical rows per layer
     size_t bytes = 0;   // reported footprint
     float* k = nullptr;

@@ -180,7 +180,8 @@ cudaError_t launch_gemv(const float* X, int ldx, const float* W, int ldw, const 
     return cudaErrorInvalidValue;
 }
 
-int gemv_argmax_blocks(int N) { return (N + kWarps * 4 - 1) / (kWarps * 4); }
+static_assert(kWarps * 4 == kGemvArgmaxRowsPerBlock, "the head's rows per block, as declared");
+int gemv_argmax_blocks(int N) { return (N + kGemvArgmaxRowsPerBlock - 1) / kGemvArgmaxRowsPerBlock; }
 
 cudaError_t launch_gemv_argmax(const float* X, int ldx, const float* W, int ldw, float* logits,
                                int ldl, int M, int N, int K, float* part_val, int* part_idx,

@@ -29,6 +29,7 @@ static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, b
     c->n_embd = n_embd;
     c->capacity = capacity;
     c->n_seq = n_seq;
+    c->contiguous = contiguous;
     c->pages_per_seq = (capacity + KV_CACHE_PAGE_ROWS - 1) / KV_CACHE_PAGE_ROWS;
     // One sequence: exactly `capacity` rows (the last page may be partial, and
     // no position reaches past capacity). A pool: whole pages per sequence.
@@ -100,13 +101,13 @@ kv_status kv_cache_set_length(kv_cache* c, int length) {
     return KV_OK;
 }
 
-static size_t phys_row(const kv_cache* c, int pos) {
-    // one-sequence caches map pages in order
-    return (size_t)pos;
-}
+// Row `pos` of a one-sequence cache: its pages are in order, so the layer is
+// one [capacity, n_embd] block. The row-level entry points serve only such
+// caches; a multi-sequence pool has no single position axis and refuses them.
+static size_t phys_row(const kv_cache* c, int pos) { return (size_t)pos; }
 
 kv_status kv_cache_write(kv_cache* c, int layer, int pos, const float* k, const float* v) {
-    if (!c || !k || !v) return KV_ERR_ARG;
+    if (!c || !k || !v || !c->contiguous) return KV_ERR_ARG;
     if (layer < 0 || layer >= c->n_layer) return KV_ERR_ARG;
     if (pos < 0) return KV_ERR_ARG;
     if (pos >= c->capacity) return KV_ERR_CAPACITY;  // checked before either store
@@ -130,12 +131,12 @@ kv_status kv_cache_advance(kv_cache* c) {
 }
 
 const float* kv_cache_keys(const kv_cache* c, int layer) {
-    if (!c || layer < 0 || layer >= c->n_layer) return nullptr;
+    if (!c || !c->contiguous || layer < 0 || layer >= c->n_layer) return nullptr;
     return c->k + (size_t)layer * c->rows * c->n_embd;
 }
 
 const float* kv_cache_values(const kv_cache* c, int layer) {
-    if (!c || layer < 0 || layer >= c->n_layer) return nullptr;
+    if (!c || !c->contiguous || layer < 0 || layer >= c->n_layer) return nullptr;
     return c->v + (size_t)layer * c->rows * c->n_embd;
 }
 
@@ -153,7 +154,8 @@ const float* kv_cache_value_row(const kv_cache* c, int layer, int pos) {
 
 kv_status kv_cache_copy_layer_to_host(const kv_cache* c, int layer, int which, float* dst,
                                       int n_rows) {
-    if (!c || !dst || layer < 0 || layer >= c->n_layer || (which != 0 && which != 1) || n_rows < 0)
+    if (!c || !dst || !c->contiguous || layer < 0 || layer >= c->n_layer || (which != 0 && which != 1) ||
+        n_rows < 0)
         return KV_ERR_ARG;
     if (n_rows > c->capacity) return KV_ERR_CAPACITY;
     const float* base = which == 0 ? kv_cache_keys(c, layer) : kv_cache_values(c, layer);

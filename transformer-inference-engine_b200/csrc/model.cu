@@ -16,6 +16,7 @@
 #include "../../include/safetensors.h"
 #include "../../include/tie_b200.h"
 #include "internal.h"
+#include "json_doc.h"
 #include "tc_gemm.h"
 
 #include <algorithm>
@@ -32,104 +33,81 @@ using namespace tie;
 
 namespace {
 
-// ------------------------------------------------------------------ JSON --
-// Just enough to read the two flat, machine-written artifacts: find "key", then
-// ':' and read the value. Mirrors what the reference's loader reads
-// (model.c:87-133), written afresh.
-const char* after_key(const char* s, const char* key) {
-    std::string pat = std::string("\"") + key + "\"";
-    const char* p = std::strstr(s, pat.c_str());
-    if (!p) return nullptr;
-    p += pat.size();
-    while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') ++p;
-    if (*p != ':') return nullptr;
-    ++p;
-    while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') ++p;
-    return p;
-}
+// ------------------------------------------------------------- artifacts --
+// config.json and the tensor inventory are parsed whole into JSON trees
+// (json_doc.h) and read by field; the inventory's "tensors" array is indexed
+// by name once per load.
 
-bool json_num(const char* s, const char* key, double* out) {
-    const char* p = after_key(s, key);
-    if (!p) return false;
-    char* end = nullptr;
-    const double v = std::strtod(p, &end);
-    if (end == p) return false;
-    *out = v;
-    return true;
-}
-
-bool json_int(const char* s, const char* key, int* out) {
-    double v;
-    if (!json_num(s, key, &v)) return false;
-    *out = (int)v;
-    return true;
-}
-
-bool json_str(const char* s, const char* key, char* out, size_t cap) {
-    const char* p = after_key(s, key);
-    if (!p || *p != '"') return false;
-    ++p;
-    size_t i = 0;
-    while (*p && *p != '"') {
-        if (i + 1 >= cap) return false;
-        out[i++] = *p++;
-    }
-    if (*p != '"') return false;
-    out[i] = 0;
-    return true;
-}
-
-bool read_text(const char* path, std::string* out) {
-    FILE* f = std::fopen(path, "rb");
-    if (!f) return false;
-    std::fseek(f, 0, SEEK_END);
-    long n = std::ftell(f);
-    if (n < 0) { std::fclose(f); return false; }
-    std::rewind(f);
-    out->resize((size_t)n);
-    size_t got = n ? std::fread(&(*out)[0], 1, (size_t)n, f) : 0;
-    out->resize(got);
-    std::fclose(f);
-    return true;
-}
-
-// One inventory record: the line that starts with {"name": "<name>",
-struct InvEntry {
-    char dtype[16] = {0};
-    char orientation[48] = {0};
-    int n_dims = 0;
-    long long dims[8] = {0};
+// A tensor as the inventory describes it.
+struct TensorInfo {
+    std::string dtype, orientation;
+    std::vector<long long> shape;
     unsigned long long file_offset = 0, nbytes = 0;
 };
 
-bool inventory_find(const std::string& inv, const char* name, InvEntry* e) {
-    std::string pat = std::string("{\"name\": \"") + name + "\",";
-    size_t at = inv.find(pat);
-    if (at == std::string::npos) return false;
-    size_t eol = inv.find('\n', at);
-    std::string line = inv.substr(at, eol == std::string::npos ? std::string::npos : eol - at);
-    *e = InvEntry();
-    if (!json_str(line.c_str(), "dtype", e->dtype, sizeof e->dtype)) return false;
-    if (!json_str(line.c_str(), "orientation", e->orientation, sizeof e->orientation)) return false;
-    double v;
-    if (!json_num(line.c_str(), "file_offset", &v)) return false;
-    e->file_offset = (unsigned long long)v;
-    if (!json_num(line.c_str(), "nbytes", &v)) return false;
-    e->nbytes = (unsigned long long)v;
-    const char* sh = after_key(line.c_str(), "shape");
-    if (!sh || *sh != '[') return false;
-    ++sh;
-    while (*sh && *sh != ']') {
-        while (*sh == ' ' || *sh == ',') ++sh;
-        if (*sh == ']') break;
-        char* end = nullptr;
-        long long d = std::strtoll(sh, &end, 10);
-        if (end == sh || e->n_dims >= 8) return false;
-        e->dims[e->n_dims++] = d;
-        sh = end;
-    }
+// Integer-valued fields are read as numbers and truncated toward zero, as a
+// C (int) conversion of the parsed value would.
+bool field_int(const json::Value& obj, const char* key, int* out) {
+    const json::Value* v = obj.get(key);
+    if (!v || !v->is_number()) return false;
+    *out = (int)v->num;
     return true;
 }
+
+bool field_u64(const json::Value& obj, const char* key, unsigned long long* out) {
+    const json::Value* v = obj.get(key);
+    if (!v || !v->is_number() || v->num < 0) return false;
+    *out = (unsigned long long)v->num;
+    return true;
+}
+
+bool field_str(const json::Value& obj, const char* key, std::string* out) {
+    const json::Value* v = obj.get(key);
+    if (!v || !v->is_string()) return false;
+    *out = v->str;
+    return true;
+}
+
+class Inventory {
+  public:
+    // false when the text is not JSON or has no "tensors" array of named records
+    bool parse(const std::string& text) {
+        if (!json::parse(text.data(), text.size(), &doc_) || doc_.kind != json::Kind::Object) return false;
+        const json::Value* list = doc_.get("tensors");
+        if (!list || list->kind != json::Kind::Array) return false;
+        for (const json::Value& rec : list->items) {
+            const json::Value* name = rec.get("name");
+            if (name && name->is_string()) by_name_.emplace(name->str, &rec);
+        }
+        return true;
+    }
+    // The record of `name`, or false when it is absent or incomplete.
+    bool find(const std::string& name, TensorInfo* t) const {
+        auto it = by_name_.find(name);
+        if (it == by_name_.end()) return false;
+        const json::Value& rec = *it->second;
+        *t = TensorInfo();
+        if (!field_str(rec, "dtype", &t->dtype) || !field_str(rec, "orientation", &t->orientation) ||
+            !field_u64(rec, "file_offset", &t->file_offset) || !field_u64(rec, "nbytes", &t->nbytes))
+            return false;
+        const json::Value* sh = rec.get("shape");
+        if (!sh || sh->kind != json::Kind::Array || sh->items.size() > 8) return false;
+        for (const json::Value& d : sh->items) {
+            if (!d.is_number()) return false;
+            t->shape.push_back((long long)d.num);
+        }
+        return true;
+    }
+    // The config values the inventory was produced against, or nullptr.
+    const json::Value* config_values() const {
+        const json::Value* cv = doc_.get("config_values_used");
+        return cv && cv->kind == json::Kind::Object ? cv : nullptr;
+    }
+
+  private:
+    json::Value doc_;
+    std::map<std::string, const json::Value*> by_name_;
+};
 
 struct Layer {
     float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
@@ -775,75 +753,135 @@ model_status finish(model* m) {
 }
 
 // --------------------------------------------------------------- loading --
-// The inventory record and the weight file header must agree with each other
-// and with the config (model.c:287-317); nothing is read here.
-model_status check_tensor(st_file* f, const std::string& inv, const char* name, int nd, long long d0,
-                          long long d1, InvEntry* out, const st_tensor** out_t) {
-    InvEntry e;
-    if (!inventory_find(inv, name, &e)) return MODEL_ERR_INVENTORY;
-    if (std::strcmp(e.dtype, "F32") != 0) return MODEL_ERR_DTYPE;
-    if (e.n_dims != nd || e.dims[0] != d0 || (nd == 2 && e.dims[1] != d1)) return MODEL_ERR_SHAPE;
+// What a tensor must be: its rank and extents from the config, F32.
+struct Expect {
+    std::string name;
+    int nd;
+    long long d0, d1;
+    size_t elems() const { return (size_t)d0 * (size_t)(nd == 2 ? d1 : 1); }
+};
+
+// Three layers of agreement are required before a tensor's bytes are read,
+// and the first disagreement decides the status (the reference's load_tensor,
+// model.c:287-317, refuses in this order):
+//   1. the inventory record against the config: absent -> INVENTORY,
+//      not F32 -> DTYPE, rank or extents -> SHAPE;
+//   2. the weight file's own header against the record: absent -> INVENTORY,
+//      not F32 -> DTYPE, extents, byte length or offset -> INVENTORY;
+//   3. the byte length against the config's element count -> SHAPE.
+model_status record_vs_config(const TensorInfo& r, const Expect& x) {
+    if (r.dtype != "F32") return MODEL_ERR_DTYPE;
+    if ((int)r.shape.size() != x.nd || r.shape[0] != x.d0 || (x.nd == 2 && r.shape[1] != x.d1))
+        return MODEL_ERR_SHAPE;
+    return MODEL_OK;
+}
+
+model_status file_vs_record(const st_tensor& t, const TensorInfo& r) {
+    if (t.dtype != ST_DTYPE_F32) return MODEL_ERR_DTYPE;
+    bool same = t.n_dims == (int)r.shape.size() && t.nbytes == r.nbytes && t.file_offset == r.file_offset;
+    for (size_t i = 0; same && i < r.shape.size(); ++i) same = t.dims[i] == (uint64_t)r.shape[i];
+    return same ? MODEL_OK : MODEL_ERR_INVENTORY;
+}
+
+model_status check_tensor(st_file* f, const Inventory& inv, const Expect& x, TensorInfo* out,
+                          const st_tensor** out_t) {
+    TensorInfo r;
+    if (!inv.find(x.name, &r)) return MODEL_ERR_INVENTORY;
+    model_status rc = record_vs_config(r, x);
+    if (rc != MODEL_OK) return rc;
     const st_tensor* t = nullptr;
-    if (st_find(f, name, &t) != ST_OK) return MODEL_ERR_INVENTORY;
-    if (t->dtype != ST_DTYPE_F32) return MODEL_ERR_DTYPE;
-    if (t->n_dims != nd) return MODEL_ERR_INVENTORY;
-    for (int i = 0; i < nd; ++i) if (t->dims[i] != e.dims[i]) return MODEL_ERR_INVENTORY;
-    if (t->nbytes != e.nbytes || t->file_offset != e.file_offset) return MODEL_ERR_INVENTORY;
-    const size_t n = (size_t)d0 * (size_t)(nd == 2 ? d1 : 1);
-    if (t->nbytes != n * sizeof(float)) return MODEL_ERR_SHAPE;
-    if (out) *out = e;
+    if (st_find(f, x.name.c_str(), &t) != ST_OK) return MODEL_ERR_INVENTORY;
+    if ((rc = file_vs_record(*t, r)) != MODEL_OK) return rc;
+    if (t->nbytes != x.elems() * sizeof(float)) return MODEL_ERR_SHAPE;
+    if (out) *out = r;
     if (out_t) *out_t = t;
     return MODEL_OK;
 }
 
-// Every tensor the forward pass uses, checked before any device work so that a
-// bad artifact is refused without touching the GPU.
-model_status check_all(st_file* f, const std::string& inv, const model_config& c) {
+// Every tensor the forward pass uses, in load order.
+std::vector<Expect> expected_tensors(const model_config& c) {
     const long long E = c.n_embd;
-    struct Want { std::string name; int nd; long long d0, d1; };
-    std::vector<Want> w = {{"wte.weight", 2, c.vocab_size, E}, {"wpe.weight", 2, c.n_ctx, E},
-                           {"ln_f.weight", 1, E, 0}, {"ln_f.bias", 1, E, 0}};
-    for (int l = 0; l < c.n_layer; ++l) {
-        const std::string p = "h." + std::to_string(l) + ".";
-        w.push_back({p + "ln_1.weight", 1, E, 0});
-        w.push_back({p + "ln_1.bias", 1, E, 0});
-        w.push_back({p + "attn.c_attn.weight", 2, E, 3 * E});
-        w.push_back({p + "attn.c_attn.bias", 1, 3 * E, 0});
-        w.push_back({p + "attn.c_proj.weight", 2, E, E});
-        w.push_back({p + "attn.c_proj.bias", 1, E, 0});
-        w.push_back({p + "ln_2.weight", 1, E, 0});
-        w.push_back({p + "ln_2.bias", 1, E, 0});
-        w.push_back({p + "mlp.c_fc.weight", 2, E, 4 * E});
-        w.push_back({p + "mlp.c_fc.bias", 1, 4 * E, 0});
-        w.push_back({p + "mlp.c_proj.weight", 2, 4 * E, E});
-        w.push_back({p + "mlp.c_proj.bias", 1, E, 0});
-    }
-    for (const Want& x : w) {
-        model_status rc = check_tensor(f, inv, x.name.c_str(), x.nd, x.d0, x.d1, nullptr, nullptr);
+    std::vector<Expect> w = {{"wte.weight", 2, c.vocab_size, E}, {"wpe.weight", 2, c.n_ctx, E},
+                             {"ln_f.weight", 1, E, 0}, {"ln_f.bias", 1, E, 0}};
+    static const struct { const char* suffix; int nd; int r0, r1; } kLayer[] = {
+        {"ln_1.weight", 1, 1, 0},        {"ln_1.bias", 1, 1, 0},
+        {"attn.c_attn.weight", 2, 1, 3}, {"attn.c_attn.bias", 1, 3, 0},
+        {"attn.c_proj.weight", 2, 1, 1}, {"attn.c_proj.bias", 1, 1, 0},
+        {"ln_2.weight", 1, 1, 0},        {"ln_2.bias", 1, 1, 0},
+        {"mlp.c_fc.weight", 2, 1, 4},    {"mlp.c_fc.bias", 1, 4, 0},
+        {"mlp.c_proj.weight", 2, 4, 1},  {"mlp.c_proj.bias", 1, 1, 0}};
+    for (int l = 0; l < c.n_layer; ++l)
+        for (const auto& k : kLayer)
+            w.push_back({"h." + std::to_string(l) + "." + k.suffix, k.nd, k.r0 * E, k.r1 * E});
+    return w;
+}
+
+// Every tensor checked before any device work, so that a bad artifact is
+// refused without touching the GPU.
+model_status check_all(st_file* f, const Inventory& inv, const model_config& c) {
+    for (const Expect& x : expected_tensors(c)) {
+        model_status rc = check_tensor(f, inv, x, nullptr, nullptr);
         if (rc != MODEL_OK) return rc;
     }
     return MODEL_OK;
 }
 
-void record(model* m, const char* name, const InvEntry& e, int transposed, const char* how) {
+void record(model* m, const char* name, const TensorInfo& e, int transposed, const char* how) {
     model_tensor_record r;
     std::memset(&r, 0, sizeof r);
     std::snprintf(r.name, sizeof r.name, "%s", name);
-    if (e.n_dims == 2) std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lldx%lld", e.dims[0], e.dims[1]);
-    else std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lld", e.dims[0]);
-    std::snprintf(r.inventory_orientation, sizeof r.inventory_orientation, "%s", e.orientation);
+    if (e.shape.size() == 2) std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lldx%lld", e.shape[0], e.shape[1]);
+    else if (!e.shape.empty()) std::snprintf(r.stored_shape, sizeof r.stored_shape, "%lld", e.shape[0]);
+    std::snprintf(r.inventory_orientation, sizeof r.inventory_orientation, "%s", e.orientation.c_str());
     r.transposed_at_load = transposed;
     std::snprintf(r.reconciliation, sizeof r.reconciliation, "%s", how);
     m->records.push_back(r);
+}
+
+// The config's model shape: every value read from the artifact, none
+// defaulted (model.c:345-365). Integer fields are numbers, the epsilon a
+// number, the activation a string naming gelu_new.
+model_status read_config(const std::string& text, model_config* cf) {
+    json::Value doc;
+    if (!json::parse(text.data(), text.size(), &doc) || doc.kind != json::Kind::Object) return MODEL_ERR_CONFIG;
+    const json::Value* eps = doc.get("layer_norm_epsilon");
+    std::string act;
+    if (!field_int(doc, "n_layer", &cf->n_layer) || !field_int(doc, "n_head", &cf->n_head) ||
+        !field_int(doc, "n_embd", &cf->n_embd) || !field_int(doc, "n_ctx", &cf->n_ctx) ||
+        !field_int(doc, "vocab_size", &cf->vocab_size) || !eps || !eps->is_number() ||
+        !field_str(doc, "activation_function", &act) || act.size() >= sizeof cf->activation_function)
+        return MODEL_ERR_CONFIG;
+    cf->layer_norm_epsilon = (float)eps->num;
+    std::snprintf(cf->activation_function, sizeof cf->activation_function, "%s", act.c_str());
+    if (cf->n_head <= 0 || cf->n_embd % cf->n_head != 0) return MODEL_ERR_CONFIG;
+    cf->head_dim = cf->n_embd / cf->n_head;
+    if (act != "gelu_new") return MODEL_ERR_CONFIG;
+    // The kernels are written for GPT-2's head width and 16-byte rows.
+    if (cf->head_dim != 64 || cf->n_embd % 4 != 0 || cf->n_layer <= 0 || cf->n_ctx <= 0 || cf->vocab_size <= 0)
+        return MODEL_ERR_CONFIG;
+    return MODEL_OK;
+}
+
+// The inventory must parse and must have been produced against the same model
+// shape as the config (model.c:372-385).
+model_status read_inventory(const std::string& text, const model_config& cf, Inventory* inv) {
+    if (!inv->parse(text)) return MODEL_ERR_INVENTORY;
+    const json::Value* cv = inv->config_values();
+    int e = 0, l = 0, h = 0, v = 0;
+    if (!cv || !field_int(*cv, "n_embd", &e) || !field_int(*cv, "n_layer", &l) || !field_int(*cv, "n_head", &h) ||
+        !field_int(*cv, "vocab_size", &v))
+        return MODEL_ERR_INVENTORY;
+    if (e != cf.n_embd || l != cf.n_layer || h != cf.n_head || v != cf.vocab_size) return MODEL_ERR_INVENTORY;
+    return MODEL_OK;
 }
 
 model_status load_impl(const char* weights_path, const char* inventory_path, const char* config_path,
                        model_cproj_reading cproj, int device, model** out) {
     if (!weights_path || !inventory_path || !config_path || !out) return MODEL_ERR_ARG;
     *out = nullptr;
-    std::string cfg_text, inv;
-    if (!read_text(config_path, &cfg_text)) return MODEL_ERR_OPEN;
-    if (!read_text(inventory_path, &inv)) return MODEL_ERR_OPEN;
+    std::string cfg_text, inv_text;
+    if (!json::read_file(config_path, &cfg_text)) return MODEL_ERR_OPEN;
+    if (!json::read_file(inventory_path, &inv_text)) return MODEL_ERR_OPEN;
 
     model* m = new (std::nothrow) model();
     if (!m) return MODEL_ERR_NOMEM;
@@ -857,39 +895,10 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
     void* pin[2] = {nullptr, nullptr};
     cudaEvent_t pin_done[2] = {nullptr, nullptr};
     int pin_cur = 0;
-    const char* c = cfg_text.c_str();
-    double eps = 0.0;
     model_config& cf = m->cfg;
-    if (!json_int(c, "n_layer", &cf.n_layer) || !json_int(c, "n_head", &cf.n_head) ||
-        !json_int(c, "n_embd", &cf.n_embd) || !json_int(c, "n_ctx", &cf.n_ctx) ||
-        !json_int(c, "vocab_size", &cf.vocab_size) || !json_num(c, "layer_norm_epsilon", &eps) ||
-        !json_str(c, "activation_function", cf.activation_function, sizeof cf.activation_function)) {
-        rc = MODEL_ERR_CONFIG;
-        goto fail;
-    }
-    cf.layer_norm_epsilon = (float)eps;
-    if (cf.n_head <= 0 || cf.n_embd % cf.n_head != 0) { rc = MODEL_ERR_CONFIG; goto fail; }
-    cf.head_dim = cf.n_embd / cf.n_head;
-    if (std::strcmp(cf.activation_function, "gelu_new") != 0) { rc = MODEL_ERR_CONFIG; goto fail; }
-    // The kernels are written for GPT-2's head width and 16-byte rows.
-    if (cf.head_dim != 64 || cf.n_embd % 4 != 0 || cf.n_layer <= 0 || cf.n_ctx <= 0 ||
-        cf.vocab_size <= 0) {
-        rc = MODEL_ERR_CONFIG;
-        goto fail;
-    }
-    {
-        const char* cv = std::strstr(inv.c_str(), "\"config_values_used\"");
-        int ie = 0, il = 0, ih = 0, iv = 0;
-        if (!cv || !json_int(cv, "n_embd", &ie) || !json_int(cv, "n_layer", &il) ||
-            !json_int(cv, "n_head", &ih) || !json_int(cv, "vocab_size", &iv)) {
-            rc = MODEL_ERR_INVENTORY;
-            goto fail;
-        }
-        if (ie != cf.n_embd || il != cf.n_layer || ih != cf.n_head || iv != cf.vocab_size) {
-            rc = MODEL_ERR_INVENTORY;
-            goto fail;
-        }
-    }
+    Inventory inv;
+    if ((rc = read_config(cfg_text, &cf)) != MODEL_OK) goto fail;
+    if ((rc = read_inventory(inv_text, cf, &inv)) != MODEL_OK) goto fail;
     if (st_open(weights_path, &f) != ST_OK) { rc = MODEL_ERR_WEIGHTS; goto fail; }
     if ((rc = check_all(f, inv, cf)) != MODEL_OK) goto fail;
 
@@ -928,10 +937,10 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
         // tensor `name` (d0 x d1 row-major in the file) to dst on the device,
         // transposed to d1 x d0 when asked: chunks through the pinned buffers,
         // asynchronous copies on the model's stream
-        auto fetch = [&](const char* name, int nd, size_t d0, size_t d1, InvEntry* out, float* dst,
+        auto fetch = [&](const char* name, int nd, size_t d0, size_t d1, TensorInfo* out, float* dst,
                          bool transpose) -> model_status {
             const st_tensor* t = nullptr;
-            model_status r = check_tensor(f, inv, name, nd, (long long)d0, (long long)d1, out, &t);
+            model_status r = check_tensor(f, inv, Expect{name, nd, (long long)d0, (long long)d1}, out, &t);
             if (r != MODEL_OK) return r;
             char* target = reinterpret_cast<char*>(transpose ? staging : dst);
             for (uint64_t off = 0; off < t->nbytes; off += kPinBytes) {
@@ -945,7 +954,7 @@ model_status load_impl(const char* weights_path, const char* inventory_path, con
             if (transpose) CU(launch_transpose(staging, dst, (int)d0, (int)d1, m->st));
             return MODEL_OK;
         };
-        InvEntry e;
+        TensorInfo e;
 #define TRY(x) do { rc = (x); if (rc != MODEL_OK) goto fail; } while (0)
         m->wte = take(V * E);
         TRY(fetch("wte.weight", 2, V, E, &e, m->wte, false));

@@ -11,12 +11,17 @@
 // library instead, so a call allocates nothing.
 //
 // The array lives in every GPU that loads this library, for the life of the
-// process (512 KiB). Its address is looked up once per device, on the first
-// call made with that device current; make that first call before any stream
-// capture. All calls share the one array: two calls that overlap on the GPU
-// (different streams, or different host threads on one device) race on it.
-// Nothing in it needs to start at zero -- every partial the final reduction
-// reads is written earlier by the same call.
+// process (512 KiB). Its address is looked up on the first call made with a
+// device current (cudaGetSymbolAddress, which also makes the device's primary
+// context current if it is not yet); make that first call before any stream
+// capture. The address is kept together with the context it belongs to and
+// looked up again when a call finds another context current (after
+// cudaDeviceReset, for instance). All calls share the one array: two calls
+// that overlap on the GPU (different streams, or different host threads on one
+// device) race on it. Nothing in it needs to start at zero -- every partial the
+// final reduction reads is written earlier by the same call.
+#include <cuda.h>
+
 #include "../../include/tie_b200.h"
 #include "common.cuh"
 
@@ -26,8 +31,7 @@ namespace {
 
 constexpr int kMaxRows = 16;          // hidden-state rows per call
 constexpr int kMaxVocab = 65536;      // vocabulary rows of the head
-constexpr int kRowsPerBlock = 16;     // the head kernel's rows per block
-constexpr int kMaxBlocks = kMaxVocab / kRowsPerBlock;
+constexpr int kMaxBlocks = kMaxVocab / tie::kGemvArgmaxRowsPerBlock;
 constexpr size_t kScratchBytes = (size_t)kMaxBlocks * kMaxRows * (sizeof(float) + sizeof(int));
 
 // per-block partial maxima: kMaxBlocks x kMaxRows values, then as many indices
@@ -35,22 +39,31 @@ static __device__ __align__(256) unsigned char g_head_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+    CUcontext ctx = nullptr;
+    void* ptr = nullptr;
+};
+ScratchAddr g_scratch[kMaxDevices];
 
-// The device address of g_head_scratch on the current device (looked up once).
+// The device address of g_head_scratch in the current device's context.
 cudaError_t scratch_for_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    CUcontext ctx = nullptr;
+    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& s = g_scratch[dev];
+    if (!s.ptr || !ctx || ctx != s.ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_head_scratch);
         if (e != cudaSuccess) return e;
-        g_scratch_addr[dev] = p;
+        if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+        s.ptr = p;
+        s.ctx = ctx;
     }
-    *out = g_scratch_addr[dev];
+    *out = s.ptr;
     return cudaSuccess;
 }
 
@@ -66,13 +79,15 @@ extern "C" model_status tie_head_argmax_noalloc(const float* x, int ldx, const f
         return MODEL_ERR_ARG;
     if (logits && ldl < vocab) return MODEL_ERR_ARG;
     if (rows > kMaxRows || vocab > kMaxVocab) return MODEL_ERR_CAPACITY;
+    // the head kernel writes one partial per (block, row): never past the array
+    const int blocks = tie::gemv_argmax_blocks(vocab);
+    if (blocks > kMaxBlocks) return MODEL_ERR_CAPACITY;
     void* scratch = nullptr;
     if (scratch_for_current_device(&scratch) != cudaSuccess) { cudaGetLastError(); return MODEL_ERR_DEVICE; }
     float* part_val = static_cast<float*>(scratch);
     int* part_idx = reinterpret_cast<int*>(static_cast<unsigned char*>(scratch) +
                                            (size_t)kMaxBlocks * kMaxRows * sizeof(float));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int blocks = tie::gemv_argmax_blocks(vocab);
     if (tie::launch_gemv_argmax(x, ldx, w, ldw, logits, ldl, rows, vocab, k, part_val, part_idx, st) !=
             cudaSuccess ||
         tie::launch_argmax_finalize(part_val, part_idx, blocks, rows, next, st) != cudaSuccess) {
