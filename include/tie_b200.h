@@ -140,14 +140,30 @@ int model_weight_format(const model *m);
 const char *tie_last_device_error(void);
 
 /* ---- how small decode steps run ------------------------------------------
- * A decode step of at most 8 sequences runs as a chain of per-layer kernels
- * linked by programmatic dependent launch: TIE_STEP_CHAINED, the default.
- * With TIE_STEP_PERSISTENT a step of at most 4 sequences (fp32 weights,
- * without attention statistics) runs as ONE persistent kernel instead. Both
- * form every sum in the same order, so they return identical logits and
- * tokens; the switch exists to compare and time them. MODEL_ERR_ARG for any
- * other value. */
-enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1 };
+ * A decode step of at most 8 sequences runs as a chain of kernels linked by
+ * programmatic dependent launch: TIE_STEP_CHAINED, the default, five per layer
+ * (LayerNorm + QKV + the step's K/V rows; attention chunk partials; their
+ * merge + attention projection + residual; LayerNorm + FC + GELU; MLP
+ * projection + residual), each matmul's weights streamed into shared memory
+ * ahead of its dependency wait. TIE_STEP_UNFUSED runs the same arithmetic as
+ * separate kernels (LayerNorm, embedding and attention merge on their own, the
+ * weights held in registers), seven per layer. With TIE_STEP_PERSISTENT a step
+ * of at most 4 sequences (fp32 weights, without attention statistics) runs as
+ * ONE persistent kernel instead. All three form every sum in the same order,
+ * so they return identical logits and tokens; the switch exists to compare
+ * and time them. MODEL_ERR_ARG for any other value. */
+enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1, TIE_STEP_UNFUSED = 2 };
+
+/* Failure drill for the bounded waits: the next decode step that runs on the
+ * default chained path (at most 8 sequences, no attention statistics) has its
+ * first matmul wait on a shared-memory barrier that nothing completes. The
+ * wait gives up after limit_ns nanoseconds, the kernel records the expiry in
+ * the model's device error flag and returns, and the step's call returns
+ * MODEL_ERR_DEVICE with the cache length unchanged; the next step runs
+ * normally. Every bounded wait of the engine's kernels reports through the
+ * same flag. MODEL_ERR_ARG for a NULL model or a zero limit. No counterpart in
+ * the reference (its CPU engine has no device waits). */
+model_status model_debug_wait_drill(model *m, uint64_t limit_ns);
 model_status model_set_step_kernel(model *m, int kind);
 
 /* Trace of one persistent decode step of `rows` (<= 4) sequences at context

@@ -210,6 +210,13 @@ cudaError_t launch_attn_decode(const float* qkv, const int32_t* lens, int B, int
                                cudaStream_t st, float* out_hi = nullptr, float* out_lo = nullptr,
                                int* counters = nullptr, int* err = nullptr);
 
+// Chunk partials of decode attention for the stream path: per (sequence b,
+// head h, 16-position chunk c) the partial (max, sum, 64 weighted sums) at
+// part[((b * H + h) * max_chunks + c) * 66]; merged by launch_stream_gemv's
+// STREAM_PRO_MERGE prologue.
+cudaError_t launch_attn_chunks(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv, int max_chunks,
+                               float* part, cudaStream_t st);
+
 // Small-batch (<= 16 rows) decode matmuls with optional LayerNorm prologue
 // (ln_g non-NULL) and PDL chaining (k_decode.cu). Weights fp32 (W), or with wt
 // 1 / 2 the bf16 / int8 copy wq (int8 with per-row scales).
@@ -219,6 +226,50 @@ cudaError_t launch_dec_gemv(const float* x, int ldx, const float* ln_g, const fl
                             int epi, const PagedKV* kv, const int32_t* lens, cudaStream_t st, int wt = WF_F32,
                             const void* wq = nullptr, const float* scale = nullptr);
 int dec_head_blocks(int V, int K, int wt, int M);
+
+// The stream path for decode steps of 1-8 rows (k_decode.cu): each matmul's
+// weights are staged in shared memory by bulk copies issued before the
+// kernel's dependency wait, and the kernel's prologue builds its input rows --
+// a copy, LayerNorm, the embedding lookup plus LayerNorm, or the merge of
+// decode-attention chunk partials -- so no separate LayerNorm, embedding or
+// merge kernel runs. Arithmetic and results are those of the separate kernels.
+enum StreamPro : int { STREAM_PRO_PLAIN = 0, STREAM_PRO_LN = 1, STREAM_PRO_EMBED_LN = 2, STREAM_PRO_MERGE = 3 };
+struct StreamParams {
+    int epi;                      // EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID, EPI_QKV_KV (ignored for the head)
+    int head;                     // the tied head: per-CTA greedy partials instead of an epilogue
+    int pro;                      // StreamPro
+    int wt;                       // WeightFormat
+    const float* x;               // input rows [M][ldx] (PLAIN, LN)
+    int ldx;
+    const float *ln_g, *ln_b;     // LN, EMBED_LN
+    float eps;
+    const int32_t* tokens;        // EMBED_LN: x = wte[tokens[m]] + wpe[lens[m]], also stored to x_out
+    const float *wte, *wpe;
+    float* x_out;
+    int V;
+    const float* apart;           // MERGE: launch_attn_chunks partials
+    int H, max_chunks;
+    const int32_t* lens;          // EMBED_LN, MERGE, EPI_QKV_KV
+    const float* W;               // [N][K] fp32, or Wq bf16 / int8 with per-row scales
+    const void* Wq;
+    const float* scale;
+    const float* bias;
+    float* y;                     // [M][ldy] output (and residual input), logits for the head (optional)
+    int ldy;
+    int M, N, K;
+    PagedKV kv;                   // EPI_QKV_KV
+    float* part_val;              // head: [grid][M] partial maxima
+    int* part_idx;
+    int* err;                     // set when a bounded wait expires
+    int stall;                    // failure drill: wait on a barrier nothing completes
+    unsigned long long wait_ns;   // the bounded waits' limit (0: one second)
+};
+// Whether every matmul of a decode step of M rows of a model of width E (and
+// MLP width 4E) runs on the stream path; the choice depends on M and E only.
+bool stream_applies(int M, int E, int wt);
+// CTAs (greedy partials) of the head's launch.
+int stream_head_blocks(int V, int K, int wt, int M);
+cudaError_t launch_stream_gemv(const StreamParams& p, cudaStream_t st);
 int dec_head_blocks_max(int V, int K);
 cudaError_t launch_dec_head(const float* x, int ldx, const float* ln_g, const float* ln_b, float eps,
                             const float* W, float* logits, int ldl, int M, int V, int K, float* part_val,

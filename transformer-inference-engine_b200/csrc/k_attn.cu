@@ -905,6 +905,61 @@ attn_decode_merge_kernel(const int32_t* __restrict__ lens, int B, int H, int max
     }
 }
 
+// Small batches ahead of the fused projection (k_decode.cu's stream path): a
+// warp per 16-position chunk of one (sequence, head), four chunks per block,
+// writing the chunk partial (max, sum, 64 weighted sums) to `part` with the
+// arithmetic of chunk_reduce; the projection kernel that follows merges them
+// in chunk order with merge_warp's formula, so the step's numbers are the
+// small-batch kernel's bit for bit. Sequence lengths are fixed for a step, so
+// every cached row (positions below the current one, written by earlier
+// steps) is loaded before the dependency wait; only the current position's
+// row and the query, which the QKV matmul just wrote, are read after it. All
+// loads go through L2 only (another kernel wrote every one of them).
+constexpr int kChunkWarps = 4;
+
+__device__ __forceinline__ void chunk_load_rows(ChunkRegs& r, const PagedKV& kv, int b, int h, int c, int lo, int hi,
+                                                int lane) {
+    const int pi = lane >> 1, half = lane & 1, E = kv.n_embd;
+    const size_t row0 = kv.row(b, c * PG);
+    if (pi >= lo && pi < hi) {
+        const float* kp = kv.k + (row0 + pi) * E + h * D;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r.k[j] = __ldcg(reinterpret_cast<const float4*>(kp + 4 * (2 * j + half)));
+    }
+    const float* vp = kv.v + row0 * E + h * D + 2 * lane;
+#pragma unroll
+    for (int i = 0; i < PG; ++i)
+        if (i >= lo && i < hi) r.v[i] = __ldcg(reinterpret_cast<const float2*>(vp + (size_t)i * E));
+}
+
+__global__ void __launch_bounds__(kChunkWarps * 32)
+attn_chunk_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ lens, int H, PagedKV kv,
+                  int max_chunks, float scale, float* __restrict__ part) {
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * kChunkWarps + warp;
+    pdl_trigger();
+    const int ctx = __ldcg(lens + b) + 1, ns = (ctx + PG - 1) / PG;
+    const bool act = c < ns && c < max_chunks;
+    const int n = act ? min(PG, ctx - c * PG) : 0;
+    const bool last = c == ns - 1;   // holds the current position
+    ChunkRegs r;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r.k[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < PG; ++i) r.v[i] = make_float2(0.f, 0.f);
+    if (act) chunk_load_rows(r, kv, b, h, c, 0, last ? n - 1 : n, lane);
+    pdl_wait();
+    if (!act) return;
+    if (last) chunk_load_rows(r, kv, b, h, c, n - 1, n, lane);
+    const int E = kv.n_embd;
+    float4 qv[8];
+    const float* q = qkv + (size_t)b * 3 * E + h * D;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qv[j] = __ldcg(reinterpret_cast<const float4*>(q + 4 * (2 * j + (lane & 1))));
+    chunk_reduce(r, qv, n, scale, lane, part + ((size_t)(b * H + h) * max_chunks + c) * PART);
+}
+
 }  // namespace
 
 // Kernels one launch_attn_decode issues with counters and without statistics:
@@ -929,6 +984,15 @@ cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float
         attn_prefill_kernel<false><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, out_hi, out_lo, nullptr);
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_attn_chunks(const float* qkv, const int32_t* lens, int B, int H, PagedKV kv, int max_chunks,
+                               float* part, cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    const float scale = (float)(1.0 / sqrt((double)D));
+    cudaError_t e = launch_pdl(attn_chunk_kernel, dim3((max_chunks + kChunkWarps - 1) / kChunkWarps, H, B),
+                               dim3(kChunkWarps * 32), 0, st, qkv, lens, H, kv, max_chunks, scale, part);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // part: B * H * max_splits * (D + 2) floats. With stats, `part` must also hold

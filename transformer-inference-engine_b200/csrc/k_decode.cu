@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "mbar.cuh"
 
 namespace tie {
 namespace {
@@ -430,6 +431,424 @@ int head_blocks_wt(int V, int K, int M) {
     return std::min(need, cap);
 }
 
+// ---------------------------------------------------------------------------
+// The stream path (launch_stream_gemv): decode matmuls of 1-8 rows with the
+// weights staged in shared memory by the bulk-copy engine.
+//
+// A CTA owns a contiguous range of weight-row groups of g rows; a group is
+// g * K contiguous weight bytes, one bulk copy into one stage of a ring. The
+// producer warp issues the first stages as soon as the CTA starts (no kernel
+// writes weights, so nothing waits for the predecessor) and refills stages as
+// the compute warps release them. A CTA takes at most ~110 KB of shared memory
+// and 288 threads, so the next kernel's CTAs are resident beside it under
+// programmatic dependent launch and have their own weights in flight while
+// this one computes: the weight stream runs ahead of the dependency chain.
+//
+// After the dependency wait the eight compute warps build the input rows in
+// shared memory (the prologue) and reduce each stage: warp w takes row w / WS
+// of the stage and K-slice w % WS, with dec_gemv_kernel's arithmetic -- lane c
+// of a slice accumulates 16-byte chunks c, c + 32, ... (elements in order),
+// an xor butterfly, then the WS slice sums in slice order. The prologue's
+// LayerNorm is the canonical order of common.cuh, and the merge of attention
+// chunk partials is merge_warp's (k_attn.cu), so a step on this path is
+// bit-identical to the chain of separate kernels.
+constexpr int kSgCompute = 8;                       // compute warps
+constexpr int kSgThreads = (kSgCompute + 1) * 32;   // + the producer warp
+constexpr int kSgMaxRows = 8;                       // activation rows
+constexpr int kSgMaxStages = 4;
+constexpr int kSgStageTarget = 24 * 1024;           // bytes of weights per stage, about
+constexpr int kSgSmemBudget = 110 * 1024;           // two consecutive kernels' CTAs share an SM
+constexpr int kSgXsMax = 48 * 1024;                 // input rows staged in shared memory up to this size
+constexpr int kAttnD = 64, kAttnPart = kAttnD + 2, kAttnPg = 16;
+
+struct SgArgs {
+    int epi, head, pro;   // DEC_* epilogue, the tied head, StreamPro
+    const float* x;
+    int ldx;
+    const float *ln_g, *ln_b;
+    float eps;
+    const int32_t* tokens;
+    const float *wte, *wpe;
+    float* x_out;
+    int V;
+    const float* apart;
+    int H, max_chunks;
+    const int32_t* lens;
+    const char* W;        // fp32 / bf16 / int8 rows, K elements each
+    const float* scale;
+    const float* bias;
+    float* y;
+    int ldy;
+    int M, N, K;
+    PagedKV kv;
+    float* part_val;
+    int* part_idx;
+    int g, ws, stages, gpc;   // rows per stage, slices per row, ring stages, groups per CTA
+    int xs;                   // input rows in shared memory (else read from global memory)
+    uint32_t stage_bytes;     // ring stride
+    uint32_t off_x, off_ring; // shared-memory offsets (bytes)
+    int* err;
+    int stall;
+    unsigned long long wait_ns;
+};
+
+// fixed part of the shared-memory layout: barriers, reductions, partial sums,
+// per-row epilogue operands; then x rows, then the ring
+struct SgFixed {
+    static constexpr uint32_t bars = 0;                                   // full[4], empty[4], never, flags
+    static constexpr uint32_t red = 128;                                  // double [2][8 rows][8 groups]
+    static constexpr uint32_t part = red + 2 * kSgMaxRows * 8 * 8;        // float [2][8 warps][8 rows]
+    static constexpr uint32_t best = part + 2 * kSgCompute * kSgMaxRows * 4;  // (float, int) [64]
+    static constexpr uint32_t lens = best + 64 * 8;                       // int [8]
+    static constexpr uint32_t epi = lens + kSgMaxRows * 4;                // bias [R], scale [R], resid [M][R]
+};
+
+__host__ __device__ inline uint32_t sg_align(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+// bounded wait; also gives up once `stop` is set (another warp gave up)
+__device__ __forceinline__ bool sg_wait(uint64_t* bar, uint32_t parity, unsigned long long limit,
+                                        volatile int* stop) {
+    if (mbar_test(bar, parity)) return true;
+    const unsigned long long t0 = gtime();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 63u) == 0) {
+            if (*stop) return false;
+            if (gtime() - t0 > limit) return false;
+        }
+    }
+}
+
+template <int WT, int MB>
+__global__ void __launch_bounds__(kSgThreads, 2)
+stream_gemv_kernel(const __grid_constant__ SgArgs a) {
+    extern __shared__ __align__(128) uint8_t sg_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(sg_smem + SgFixed::bars);
+    uint64_t* empty = full + kSgMaxStages;
+    uint64_t* never = empty + kSgMaxStages;
+    // stop: any warp gave up (producer or compute). quit[i & 1]: a compute warp
+    // gave up in stage i; it is set only before stage i's compute barrier and
+    // read only after it (never cleared), so every compute warp reads the same
+    // value and they leave the stage loop together
+    volatile int* stop = reinterpret_cast<volatile int*>(never + 1);
+    volatile int* quit = stop + 1;
+    double* s_red = reinterpret_cast<double*>(sg_smem + SgFixed::red);
+    float* s_part = reinterpret_cast<float*>(sg_smem + SgFixed::part);
+    float* s_bv = reinterpret_cast<float*>(sg_smem + SgFixed::best);
+    int* s_bi = reinterpret_cast<int*>(sg_smem + SgFixed::best + 64 * 4);
+    int* s_lens = reinterpret_cast<int*>(sg_smem + SgFixed::lens);
+    const int R = a.gpc * a.g;   // weight rows of this CTA's range
+    float* s_bias = reinterpret_cast<float*>(sg_smem + SgFixed::epi);
+    float* s_scale = s_bias + R;
+    float* s_res = s_scale + R;
+    float* x_s = reinterpret_cast<float*>(sg_smem + a.off_x);
+    uint8_t* ring = sg_smem + a.off_ring;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int EPI = a.head ? (int)DEC_HEAD : a.epi, PRO = a.pro;
+    constexpr int EPC = elems_per_chunk<WT>();
+    constexpr int BPE = WT == 0 ? 4 : (WT == 1 ? 2 : 1);
+    const int M = a.M, K = a.K, S = a.stages;
+    const int g0 = blockIdx.x * a.gpc;                                   // first group
+    const int ng = max(0, min(a.gpc, (a.N + a.g - 1) / a.g - g0));      // groups of this CTA
+    const int row_base = g0 * a.g;
+    const unsigned long long limit = a.wait_ns ? a.wait_ns : kWaitNs;
+
+    if (tid == 0) {
+        for (int s = 0; s < kSgMaxStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kSgCompute);
+        }
+        mbar_init(never, 1);
+        *stop = 0;
+        quit[0] = 0;
+        quit[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == kSgCompute) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t pol = evict_first_policy();
+            const size_t row_bytes = (size_t)K * BPE;
+            int issued = 0;
+            for (int i = 0; i < ng; ++i) {
+                const int slot = i % S;
+                if (i >= S && !sg_wait(&empty[slot], (uint32_t)((i / S) - 1) & 1u, limit, stop)) {
+                    *stop = 1;
+                    atomicExch(a.err, 1);
+                    break;
+                }
+                const int row0 = (g0 + i) * a.g;
+                const uint32_t bytes = (uint32_t)(min(a.g, a.N - row0) * row_bytes);
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_load(ring + (size_t)slot * a.stage_bytes, a.W + (size_t)row0 * row_bytes, bytes, &full[slot], pol);
+                ++issued;
+            }
+            // every copy this thread started has landed before the CTA may exit
+            for (int j = issued > S ? issued - S : 0; j < issued; ++j)
+                if (!sg_wait(&full[j % S], (uint32_t)(j / S) & 1u, limit, stop)) {
+                    const unsigned long long t0 = gtime();
+                    while (!mbar_try(&full[j % S], (uint32_t)(j / S) & 1u) && gtime() - t0 < limit) {
+                    }
+                }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ compute
+    // operands that no earlier kernel writes: before the dependency wait
+    if (EPI != DEC_HEAD) {
+        for (int t = tid; t < R; t += kSgCompute * 32)
+            s_bias[t] = row_base + t < a.N ? __ldg(a.bias + row_base + t) : 0.f;
+    }
+    if constexpr (WT == 2) {
+        for (int t = tid; t < R; t += kSgCompute * 32)
+            s_scale[t] = row_base + t < a.N ? __ldg(a.scale + row_base + t) : 1.f;
+    }
+    float gam[8], bet[8];   // LayerNorm gain and shift of elements tid + 256 j
+    if (PRO == STREAM_PRO_LN || PRO == STREAM_PRO_EMBED_LN) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + 256 * j;
+            gam[j] = i < K ? __ldg(a.ln_g + i) : 0.f;
+            bet[j] = i < K ? __ldg(a.ln_b + i) : 0.f;
+        }
+    }
+    pdl_wait();
+
+    // ----------------------------------------------------------- prologue
+    if (tid < M && (PRO == STREAM_PRO_EMBED_LN || PRO == STREAM_PRO_MERGE || EPI == DEC_QKV_KV))
+        s_lens[tid] = __ldcg(a.lens + tid);
+    if (EPI == DEC_BIAS_RESID) {
+        for (int t = tid; t < M * R; t += kSgCompute * 32) {
+            const int m = t / R, r = t % R;
+            s_res[t] = row_base + r < a.N ? __ldcg(a.y + (size_t)m * a.ldy + row_base + r) : 0.f;
+        }
+    }
+    const int K4 = K >> 2;
+    if (PRO == STREAM_PRO_PLAIN || PRO == STREAM_PRO_LN) {
+        if (a.xs)
+            for (int t = tid; t < M * K4; t += kSgCompute * 32) {
+                const int m = t / K4, c = t % K4;
+                reinterpret_cast<float4*>(x_s)[t] = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx) + c);
+            }
+    }
+    if (PRO == STREAM_PRO_EMBED_LN) {
+        bar_sync(1, kSgCompute * 32);   // s_lens
+        for (int t = tid; t < M * K4; t += kSgCompute * 32) {
+            const int m = t / K4, c = t % K4;
+            const int id = __ldcg(a.tokens + m);
+            float4 v;
+            if ((unsigned)id >= (unsigned)a.V) {
+                v = make_float4(NAN, NAN, NAN, NAN);
+            } else {
+                const float4 e = __ldg(reinterpret_cast<const float4*>(a.wte + (size_t)id * K) + c);
+                const float4 p = __ldg(reinterpret_cast<const float4*>(a.wpe + (size_t)s_lens[m] * K) + c);
+                v = make_float4(__fadd_rn(e.x, p.x), __fadd_rn(e.y, p.y), __fadd_rn(e.z, p.z), __fadd_rn(e.w, p.w));
+            }
+            reinterpret_cast<float4*>(x_s)[t] = v;
+            if (blockIdx.x == 0) reinterpret_cast<float4*>(a.x_out + (size_t)m * K)[c] = v;
+        }
+    }
+    if (PRO == STREAM_PRO_LN || PRO == STREAM_PRO_EMBED_LN) {
+        // LayerNorm of every row in place, the canonical order: thread tid is
+        // virtual lane tid, warp w group w
+        bar_sync(1, kSgCompute * 32);
+        double acc[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            acc[m] = 0.0;
+            if (m < M)
+                for (int i = tid; i < K; i += 256) acc[m] = __dadd_rn(acc[m], (double)x_s[m * K + i]);
+            acc[m] = ln_warp_sum_d(acc[m]);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) s_red[m * 8 + warp] = acc[m];
+        bar_sync(1, kSgCompute * 32);
+        double mean[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            double S_ = s_red[m * 8];
+#pragma unroll
+            for (int w = 1; w < kLnGroups; ++w) S_ = __dadd_rn(S_, s_red[m * 8 + w]);
+            mean[m] = S_ / (double)K;
+            acc[m] = 0.0;
+            if (m < M)
+                for (int i = tid; i < K; i += 256) {
+                    const double d = __dadd_rn((double)x_s[m * K + i], -mean[m]);
+                    acc[m] = __dadd_rn(acc[m], __dmul_rn(d, d));
+                }
+            acc[m] = ln_warp_sum_d(acc[m]);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) s_red[kSgMaxRows * 8 + m * 8 + warp] = acc[m];
+        bar_sync(1, kSgCompute * 32);
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            if (m >= M) break;
+            double V_ = s_red[kSgMaxRows * 8 + m * 8];
+#pragma unroll
+            for (int w = 1; w < kLnGroups; ++w) V_ = __dadd_rn(V_, s_red[kSgMaxRows * 8 + m * 8 + w]);
+            const float inv = (float)(1.0 / sqrt(__dadd_rn(V_ / (double)K, (double)a.eps)));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = tid + 256 * j;
+                if (i < K) x_s[m * K + i] = ln_apply(x_s[m * K + i], mean[m], inv, gam[j], bet[j]);
+            }
+        }
+    }
+    if (PRO == STREAM_PRO_MERGE) {
+        // attention rows from the chunk partials: warp per (row, head), the
+        // arithmetic of merge_warp
+        bar_sync(1, kSgCompute * 32);   // s_lens
+        for (int p = warp; p < M * a.H; p += kSgCompute) {
+            const int m = p / a.H, h = p % a.H;
+            const int ns = (s_lens[m] + 1 + kAttnPg - 1) / kAttnPg;
+            const float* P = a.apart + (size_t)(m * a.H + h) * a.max_chunks * kAttnPart;
+            float mx = -INFINITY;
+            for (int k = lane; k < ns; k += 32) mx = fmaxf(mx, __ldcg(P + (size_t)k * kAttnPart));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float lt = 0.f, o0 = 0.f, o1 = 0.f;
+            for (int k0 = 0; k0 < ns; k0 += 8) {
+                float2 ml[8], ov[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k0 + k < ns) {
+                        ml[k] = __ldcg(reinterpret_cast<const float2*>(P + (size_t)(k0 + k) * kAttnPart));
+                        ov[k] = __ldcg(reinterpret_cast<const float2*>(P + (size_t)(k0 + k) * kAttnPart + 2 + 2 * lane));
+                    }
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k0 + k < ns) {
+                        const float cf = expf(ml[k].x - mx);
+                        lt = fmaf(ml[k].y, cf, lt);
+                        o0 = fmaf(ov[k].x, cf, o0);
+                        o1 = fmaf(ov[k].y, cf, o1);
+                    }
+            }
+            *reinterpret_cast<float2*>(x_s + (size_t)m * K + h * kAttnD + 2 * lane) = make_float2(o0 / lt, o1 / lt);
+        }
+    }
+    bar_sync(1, kSgCompute * 32);
+
+    // failure drill: a barrier that nothing completes; the bounded wait expires
+    if (a.stall && !sg_wait(never, 0, limit, stop)) {
+        if (tid == 0) atomicExch(a.err, 1);
+        quit[0] = 1;
+        *stop = 1;
+    }
+
+    // -------------------------------------------------------------- stages
+    const int K4c = K / EPC;                              // 16-byte chunks per row
+    const int slice = (K4c + a.ws - 1) / a.ws;
+    const int my_r = warp / a.ws, my_s = warp % a.ws;
+    const int c0 = my_s * slice, c1 = min(K4c, c0 + slice);
+    float bv = 0.f;   // head: this thread's best (value, index) and the NaN-at-0 flag
+    int bi = -1;
+    bool nan0 = false;
+    for (int i = 0; i < ng; ++i) {
+        const int slot = i % S, buf = i & 1;
+        const int row0 = (g0 + i) * a.g, rows = min(a.g, a.N - row0);
+        const bool ok = sg_wait(&full[slot], (uint32_t)(i / S) & 1u, limit, stop);
+        if (!ok) {
+            quit[buf] = 1;
+            *stop = 1;
+            if (lane == 0) atomicExch(a.err, 1);
+        }
+        float acc[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) acc[m] = 0.f;
+        if (ok && my_r < rows) {
+            const uint8_t* wrow = ring + (size_t)slot * a.stage_bytes + (size_t)my_r * K * BPE;
+            for (int c = c0 + lane; c < c1; c += 32) {
+                const float4 wv = *reinterpret_cast<const float4*>(wrow + (size_t)c * 16);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    if (m < M) {
+                        float t = acc[m];
+#pragma unroll
+                        for (int q4 = 0; q4 < EPC / 4; ++q4) {
+                            const size_t xi = (size_t)m * (a.xs ? K : a.ldx) + (size_t)c * EPC + 4 * q4;
+                            const float4 xv = a.xs ? *reinterpret_cast<const float4*>(x_s + xi)
+                                                   : __ldcg(reinterpret_cast<const float4*>(a.x + xi));
+                            t = fmaf(chunk_elem<WT>(wv, 4 * q4 + 0), xv.x, t);
+                            t = fmaf(chunk_elem<WT>(wv, 4 * q4 + 1), xv.y, t);
+                            t = fmaf(chunk_elem<WT>(wv, 4 * q4 + 2), xv.z, t);
+                            t = fmaf(chunk_elem<WT>(wv, 4 * q4 + 3), xv.w, t);
+                        }
+                        acc[m] = t;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            float v = acc[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            acc[m] = v;
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) s_part[(buf * kSgCompute + warp) * kSgMaxRows + m] = acc[m];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        bar_sync(1, kSgCompute * 32);
+        if (quit[buf]) break;
+        // epilogue: thread t finishes (row t / M, activation row t % M)
+        if (tid < rows * M) {
+            const int rr = tid / M, m = tid % M, j = row0 + rr, lr = i * a.g + rr;
+            float sum = s_part[(buf * kSgCompute + rr * a.ws) * kSgMaxRows + m];
+            for (int k = 1; k < a.ws; ++k) sum += s_part[(buf * kSgCompute + rr * a.ws + k) * kSgMaxRows + m];
+            if constexpr (WT == 2) sum = sum * s_scale[lr];
+            if (EPI == DEC_HEAD) {
+                if (a.y) a.y[(size_t)m * a.ldy + j] = sum;
+                if (j == 0 && !(sum == sum)) nan0 = true;
+                else if (sum == sum && beats(sum, j, bv, bi)) { bv = sum; bi = j; }
+            } else {
+                float v = __fadd_rn(sum, s_bias[lr]);
+                if (EPI == DEC_BIAS_GELU) v = gelu_new_ref(v);
+                if (EPI == DEC_BIAS_RESID) v = __fadd_rn(s_res[m * R + lr], v);
+                a.y[(size_t)m * a.ldy + j] = v;
+                if (EPI == DEC_QKV_KV) {
+                    const int E = a.kv.n_embd;
+                    if (j >= E) {
+                        const size_t row = a.kv.row(m, s_lens[m]);
+                        if (j < 2 * E) a.kv.k[row * E + (j - E)] = v;
+                        else a.kv.v[row * E + (j - 2 * E)] = v;
+                    }
+                }
+            }
+        }
+    }
+    if (EPI == DEC_HEAD) {
+        // this CTA's best per activation row: the g threads of a row, in order
+        const int nthr = a.g * M;
+        if (tid < nthr) {
+            s_bv[tid] = bv;
+            s_bi[tid] = nan0 ? -2 : bi;
+        }
+        bar_sync(1, kSgCompute * 32);
+        if (tid < M) {
+            float b2 = 0.f;
+            int i2 = -1;
+            bool n2 = false;
+            for (int t = tid; t < nthr; t += M) {
+                if (s_bi[t] == -2) n2 = true;
+                else if (s_bi[t] >= 0 && beats(s_bv[t], s_bi[t], b2, i2)) { b2 = s_bv[t]; i2 = s_bi[t]; }
+            }
+            a.part_val[(size_t)blockIdx.x * M + tid] = b2;
+            a.part_idx[(size_t)blockIdx.x * M + tid] = n2 ? -2 : i2;
+        }
+    }
+}
+
 }  // namespace
 
 // Blocks (one partial best per block and row) of the tied head's launch for
@@ -443,6 +862,122 @@ int dec_head_blocks_max(int V, int K) {
     for (int wt : {0, 1, 2})
         for (int M : {1, 2, 4, 8, 16}) n = std::max(n, dec_head_blocks(V, K, wt, M));
     return n;
+}
+
+// ------------------------------------------------------- the stream path --
+namespace {
+
+struct SgGeom {
+    int g, ws, gpc, grid, stages, xs;
+    uint32_t stage_bytes, off_x, off_ring, smem;
+};
+
+// The launch geometry of one stream-path matmul, from its shape, weight format
+// and kinds only (never from which rows are in the batch beyond their count):
+// false when the path cannot run it.
+bool sg_geometry(int M, int N, int K, int wt, int pro, int epi, bool head, SgGeom* o) {
+    const int bpe = wt == 0 ? 4 : (wt == 1 ? 2 : 1);
+    const int epc = 16 / bpe;
+    if (M < 1 || M > kSgMaxRows || N < 1 || K < 4 || K % epc || K % 4) return false;
+    const int k4c = K / epc;
+    if (k4c > (wt == 0 ? 2048 : 1024)) return false;
+    if ((pro == STREAM_PRO_LN || pro == STREAM_PRO_EMBED_LN) && K > 8 * 256) return false;
+    const int ws = k4c <= 256 ? 1 : 4;      // dec_dispatch's slicing
+    const int row_bytes = K * bpe;
+    const int g = std::max(1, std::min(kSgStageTarget / row_bytes, kSgCompute / ws));
+    const int ng = (N + g - 1) / g;
+    const int sms = sm_count();
+    const int gpc = (ng + sms - 1) / sms;
+    const int R = gpc * g;
+    const uint32_t xbytes = (uint32_t)M * K * 4;
+    const int xs = xbytes <= (uint32_t)kSgXsMax;
+    if (pro != STREAM_PRO_PLAIN && !xs) return false;
+    // per-row epilogue operands: R bias slots, R scale slots, then M x R residuals
+    const uint32_t epi_span = 4u * (2 * R + (!head && epi == EPI_BIAS_RESID ? M * R : 0));
+    o->g = g;
+    o->ws = ws;
+    o->gpc = gpc;
+    o->grid = (ng + gpc - 1) / gpc;
+    o->xs = xs;
+    o->off_x = sg_align(SgFixed::epi + epi_span, 128);
+    o->off_ring = sg_align(o->off_x + (xs ? xbytes : 0), 128);
+    o->stage_bytes = sg_align((uint32_t)(g * row_bytes), 128);
+    const int budget = kSgSmemBudget - (int)o->off_ring;
+    o->stages = std::min({kSgMaxStages, gpc, budget / (int)o->stage_bytes});
+    if (o->stages < 1) return false;
+    o->smem = o->off_ring + (uint32_t)o->stages * o->stage_bytes;
+    return true;
+}
+
+template <int WT, int MB>
+cudaError_t sg_launch(const SgArgs& a, const SgGeom& g, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(stream_gemv_kernel<WT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSgSmemBudget);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaError_t e = launch_pdl(stream_gemv_kernel<WT, MB>, dim3(g.grid), dim3(kSgThreads), g.smem, st, a);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int WT>
+cudaError_t sg_launch_m(const SgArgs& a, const SgGeom& g, cudaStream_t st) {
+    if (a.M <= 1) return sg_launch<WT, 1>(a, g, st);
+    if (a.M <= 2) return sg_launch<WT, 2>(a, g, st);
+    if (a.M <= 4) return sg_launch<WT, 4>(a, g, st);
+    return sg_launch<WT, 8>(a, g, st);
+}
+
+}  // namespace
+
+bool stream_applies(int M, int E, int wt) {
+    SgGeom g;
+    return sg_geometry(M, 3 * E, E, wt, STREAM_PRO_EMBED_LN, EPI_QKV_KV, false, &g) &&
+           sg_geometry(M, E, E, wt, STREAM_PRO_MERGE, EPI_BIAS_RESID, false, &g) &&
+           sg_geometry(M, 4 * E, E, wt, STREAM_PRO_LN, EPI_BIAS_GELU, false, &g) &&
+           sg_geometry(M, E, 4 * E, wt, STREAM_PRO_PLAIN, EPI_BIAS_RESID, false, &g) &&
+           sg_geometry(M, 50257, E, wt, STREAM_PRO_LN, EPI_STORE, true, &g);
+}
+
+int stream_head_blocks(int V, int K, int wt, int M) {
+    SgGeom g;
+    return sg_geometry(M, V, K, wt, STREAM_PRO_LN, EPI_STORE, true, &g) ? g.grid : 0;
+}
+
+cudaError_t launch_stream_gemv(const StreamParams& p, cudaStream_t st) {
+    if (p.wt < 0 || p.wt > 2 || (p.wt == 0 && !p.W) || (p.wt != 0 && !p.Wq) || (p.wt == 2 && !p.scale) || !p.err)
+        return cudaErrorInvalidValue;
+    if (!p.head && p.epi != EPI_BIAS && p.epi != EPI_BIAS_GELU && p.epi != EPI_BIAS_RESID && p.epi != EPI_QKV_KV)
+        return cudaErrorInvalidValue;
+    if (p.head && (!p.part_val || !p.part_idx)) return cudaErrorInvalidValue;
+    if (!p.head && (!p.bias || !p.y)) return cudaErrorInvalidValue;
+    if ((p.pro == STREAM_PRO_LN || p.pro == STREAM_PRO_EMBED_LN) && (!p.ln_g || !p.ln_b)) return cudaErrorInvalidValue;
+    if (p.pro == STREAM_PRO_EMBED_LN && (!p.tokens || !p.wte || !p.wpe || !p.x_out || !p.lens)) return cudaErrorInvalidValue;
+    if (p.pro == STREAM_PRO_MERGE && (!p.apart || !p.lens || p.H * kAttnD != p.K)) return cudaErrorInvalidValue;
+    if ((p.pro == STREAM_PRO_PLAIN || p.pro == STREAM_PRO_LN) && (!p.x || (p.ldx & 3))) return cudaErrorInvalidValue;
+    if (p.epi == EPI_QKV_KV && !p.head && !p.lens) return cudaErrorInvalidValue;
+    SgGeom g;
+    if (!sg_geometry(p.M, p.N, p.K, p.wt, p.pro, p.epi, p.head != 0, &g)) return cudaErrorInvalidValue;
+    SgArgs a{};
+    a.epi = p.epi == EPI_BIAS ? DEC_BIAS : p.epi == EPI_BIAS_GELU ? DEC_BIAS_GELU
+          : p.epi == EPI_BIAS_RESID ? DEC_BIAS_RESID : DEC_QKV_KV;
+    a.head = p.head;
+    a.pro = p.pro;
+    a.x = p.x; a.ldx = p.ldx; a.ln_g = p.ln_g; a.ln_b = p.ln_b; a.eps = p.eps;
+    a.tokens = p.tokens; a.wte = p.wte; a.wpe = p.wpe; a.x_out = p.x_out; a.V = p.V;
+    a.apart = p.apart; a.H = p.H; a.max_chunks = p.max_chunks; a.lens = p.lens;
+    a.W = p.wt == 0 ? reinterpret_cast<const char*>(p.W) : reinterpret_cast<const char*>(p.Wq);
+    a.scale = p.scale; a.bias = p.bias; a.y = p.y; a.ldy = p.ldy;
+    a.M = p.M; a.N = p.N; a.K = p.K; a.kv = p.kv;
+    a.part_val = p.part_val; a.part_idx = p.part_idx;
+    a.g = g.g; a.ws = g.ws; a.stages = g.stages; a.gpc = g.gpc; a.xs = g.xs;
+    a.stage_bytes = g.stage_bytes; a.off_x = g.off_x; a.off_ring = g.off_ring;
+    a.err = p.err; a.stall = p.stall; a.wait_ns = p.wait_ns;
+    if (p.wt == 1) return sg_launch_m<1>(a, g, st);
+    if (p.wt == 2) return sg_launch_m<2>(a, g, st);
+    return sg_launch_m<0>(a, g, st);
 }
 
 // y = x . W^T (+ epilogue) for M <= 16 rows, chained with PDL. Weights fp32

@@ -242,6 +242,9 @@ struct model {
     int step_slots[5] = {0, 0, 0, 0, 0};
     int step_grid = 0;
     uint64_t launches = 0;
+    // failure drill: the next decode step's first matmul waits on a barrier
+    // nothing completes, for at most drill_ns (model_debug_wait_drill)
+    unsigned long long drill_ns = 0;
 };
 
 namespace {
@@ -542,7 +545,94 @@ model_status build_weight_set(model* m, int fmt) {
     return MODEL_OK;
 }
 
+// The stream path of a decode step of B <= 8 sequences (k_decode.cu): five
+// kernels per layer, LayerNorm, embedding and the attention merge folded into
+// the matmuls' prologues, every matmul's weights in flight before its
+// dependency wait.                                           model.c:794-868
+bool use_stream(const model* m, int B) {
+    return !m->stats_on && m->step_kind != TIE_STEP_UNFUSED && B <= kGemvRows &&
+           stream_applies(B, m->cfg.n_embd, m->wfmt);
+}
+
+StreamParams stream_base(model* m, int B) {
+    StreamParams p{};
+    p.M = B;
+    p.eps = m->cfg.layer_norm_epsilon;
+    p.lens = m->d_lens;
+    p.err = m->d_err;
+    return p;
+}
+
+void stream_weights(StreamParams& p, const float* W, const QMat& q, const float* bias) {
+    p.W = W;
+    p.wt = q.wt;
+    p.Wq = q.q;
+    p.scale = q.s;
+    p.bias = bias;
+}
+
+model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
+    const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size;
+    cudaStream_t st = m->st;
+    const int max_chunks = attn_decode_max_splits(cache->capacity);
+    const StreamParams base = stream_base(m, B);
+    for (int l = 0; l < m->cfg.n_layer; ++l) {
+        const Layer& w = m->layers[l];
+        const PagedKV view = layer_view(cache, l);
+        // LayerNorm 1 (layer 0: of the embedding, also stored as x) + QKV + this step's K/V rows
+        StreamParams p = base;
+        p.epi = EPI_QKV_KV;
+        p.pro = l == 0 ? STREAM_PRO_EMBED_LN : STREAM_PRO_LN;
+        p.x = m->x; p.ldx = E; p.ln_g = w.ln1_w; p.ln_b = w.ln1_b;
+        p.tokens = m->d_tokens; p.wte = m->wte; p.wpe = m->wpe; p.x_out = m->x; p.V = V;
+        stream_weights(p, w.qkv_w, qmat(m, l, 0), w.qkv_b);
+        p.y = m->qkv; p.ldy = 3 * E; p.N = 3 * E; p.K = E; p.kv = view;
+        if (l == 0 && m->drill_ns) { p.stall = 1; p.wait_ns = m->drill_ns; }
+        LAUNCH(launch_stream_gemv(p, st));
+        // attention: chunk partials
+        LAUNCH(launch_attn_chunks(m->qkv, m->d_lens, B, H, view, max_chunks, m->d_part, st));
+        // their merge + attention projection + residual
+        p = base;
+        p.epi = EPI_BIAS_RESID;
+        p.pro = STREAM_PRO_MERGE;
+        p.apart = m->d_part; p.H = H; p.max_chunks = max_chunks;
+        stream_weights(p, w.proj_w, qmat(m, l, 1), w.proj_b);
+        p.y = m->x; p.ldy = E; p.N = E; p.K = E;
+        LAUNCH(launch_stream_gemv(p, st));
+        // LayerNorm 2 + FC + GELU
+        p = base;
+        p.epi = EPI_BIAS_GELU;
+        p.pro = STREAM_PRO_LN;
+        p.x = m->x; p.ldx = E; p.ln_g = w.ln2_w; p.ln_b = w.ln2_b;
+        stream_weights(p, w.fc_w, qmat(m, l, 2), w.fc_b);
+        p.y = m->ff; p.ldy = 4 * E; p.N = 4 * E; p.K = E;
+        LAUNCH(launch_stream_gemv(p, st));
+        // MLP projection + residual
+        p = base;
+        p.epi = EPI_BIAS_RESID;
+        p.pro = STREAM_PRO_PLAIN;
+        p.x = m->ff; p.ldx = 4 * E;
+        stream_weights(p, w.mlp_w, qmat(m, l, 3), w.mlp_b);
+        p.y = m->x; p.ldy = E; p.N = E; p.K = 4 * E;
+        LAUNCH(launch_stream_gemv(p, st));
+    }
+    // LayerNorm f + the tied head with per-CTA greedy partials
+    const QMat qh = qmat(m, m->cfg.n_layer, 0);
+    StreamParams p = base;
+    p.head = 1;
+    p.pro = STREAM_PRO_LN;
+    p.x = m->x; p.ldx = E; p.ln_g = m->lnf_w; p.ln_b = m->lnf_b;
+    stream_weights(p, m->wte, qh, nullptr);
+    p.y = m->logits; p.ldy = V; p.N = V; p.K = E;
+    p.part_val = m->d_am_val; p.part_idx = m->d_am_idx;
+    LAUNCH(launch_stream_gemv(p, st));
+    LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, stream_head_blocks(V, E, qh.wt, B), B, m->d_next, st));
+    if (advance) LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
+    return MODEL_OK;
+}
+
 model_status run_decode(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
+    if (use_stream(m, B)) return run_decode_stream(m, B, cache, advance, out, ld_out);
     const int E = m->cfg.n_embd, H = m->cfg.n_head, V = m->cfg.vocab_size;
     const float eps = m->cfg.layer_norm_epsilon;
     cudaStream_t st = m->st;
@@ -692,6 +782,12 @@ model_status run_step(model* m, int B, kv_cache* cache, bool advance, int32_t* o
 
 model_status decode_step(model* m, int B, kv_cache* cache, bool advance, int32_t* out, int ld_out) {
     if (m->stats_on) return run_decode(m, B, cache, advance, out, ld_out);
+    if (m->drill_ns && use_stream(m, B)) {
+        // one step run directly (not from a graph), then the drill is over
+        model_status rc = run_decode(m, B, cache, advance, out, ld_out);
+        m->drill_ns = 0;
+        return rc;
+    }
     if (use_step(m, B, cache)) return run_step(m, B, cache, advance, out, ld_out);
     const GraphKey key{B, cache, advance, out, ld_out};
     auto it = m->graphs.find(key);
@@ -1507,8 +1603,15 @@ model_status model_set_weight_format(model* m, int fmt) {
 
 int model_weight_format(const model* m) { return m ? m->wfmt : -1; }
 
+model_status model_debug_wait_drill(model* m, uint64_t limit_ns) {
+    if (!m || limit_ns == 0) return MODEL_ERR_ARG;
+    m->drill_ns = limit_ns;
+    return MODEL_OK;
+}
+
 model_status model_set_step_kernel(model* m, int kind) {
-    if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED)) return MODEL_ERR_ARG;
+    if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED && kind != TIE_STEP_UNFUSED))
+        return MODEL_ERR_ARG;
     if (kind != m->step_kind) drop_graphs(m);
     m->step_kind = kind;
     return MODEL_OK;
@@ -1541,7 +1644,49 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
     CU(cudaMemsetAsync(m->xb_lo, 0, R * E * sizeof(float), st));
     CU(cudaMemsetAsync(m->ff_hi, 0, R * 4 * E * sizeof(float), st));
     CU(cudaMemsetAsync(m->ff_lo, 0, R * 4 * E * sizeof(float), st));
+    const bool stream = use_stream(m, B);
+    const StreamParams sbase = stream_base(m, B);
     auto once = [&]() -> model_status {
+        if (stream && kernel >= TIE_KERNEL_DECODE_ATTENTION && kernel <= TIE_KERNEL_DECODE_HEAD) {
+            StreamParams p = sbase;
+            switch (kernel) {
+                case TIE_KERNEL_DECODE_ATTENTION:
+                    CU(launch_attn_chunks(m->qkv, m->d_lens, B, H, view, splits, m->d_part, st));
+                    return MODEL_OK;
+                case TIE_KERNEL_DECODE_QKV:
+                    p.epi = EPI_QKV_KV; p.pro = STREAM_PRO_LN;
+                    p.x = m->x; p.ldx = E; p.ln_g = w.ln1_w; p.ln_b = w.ln1_b;
+                    stream_weights(p, w.qkv_w, qmat(m, 0, 0), w.qkv_b);
+                    p.y = m->qkv; p.ldy = 3 * E; p.N = 3 * E; p.K = E; p.kv = view;
+                    break;
+                case TIE_KERNEL_DECODE_FC:
+                    p.epi = EPI_BIAS_GELU; p.pro = STREAM_PRO_LN;
+                    p.x = m->x; p.ldx = E; p.ln_g = w.ln2_w; p.ln_b = w.ln2_b;
+                    stream_weights(p, w.fc_w, qmat(m, 0, 2), w.fc_b);
+                    p.y = m->ff; p.ldy = 4 * E; p.N = 4 * E; p.K = E;
+                    break;
+                case TIE_KERNEL_DECODE_MLP_PROJ:
+                    p.epi = EPI_BIAS_RESID; p.pro = STREAM_PRO_PLAIN;
+                    p.x = m->ff; p.ldx = 4 * E;
+                    stream_weights(p, w.mlp_w, qmat(m, 0, 3), w.mlp_b);
+                    p.y = m->x; p.ldy = E; p.N = E; p.K = 4 * E;
+                    break;
+                default: {   // the head
+                    const QMat qh = qmat(m, m->cfg.n_layer, 0);
+                    p.head = 1; p.pro = STREAM_PRO_LN;
+                    p.x = m->x; p.ldx = E; p.ln_g = m->lnf_w; p.ln_b = m->lnf_b;
+                    stream_weights(p, m->wte, qh, nullptr);
+                    p.y = m->logits; p.ldy = V; p.N = V; p.K = E;
+                    p.part_val = m->d_am_val; p.part_idx = m->d_am_idx;
+                    CU(launch_stream_gemv(p, st));
+                    CU(launch_argmax_finalize(m->d_am_val, m->d_am_idx, stream_head_blocks(V, E, qh.wt, B), B,
+                                              m->d_next, st));
+                    return MODEL_OK;
+                }
+            }
+            CU(launch_stream_gemv(p, st));
+            return MODEL_OK;
+        }
         switch (kernel) {
             case TIE_KERNEL_DECODE_ATTENTION:
                 CU(launch_attn_decode(m->qkv, m->d_lens, B, H, view, splits, m->d_part, small ? m->attn : nullptr,

@@ -45,21 +45,39 @@ struct ScratchAddr {
 };
 ScratchAddr g_scratch[kMaxDevices];
 
+// cuCtxGetCurrent through the runtime's driver entry point (the library does
+// not link the driver library directly, so it loads on machines without one)
+CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        fn = reinterpret_cast<Fn>(p);
+    }
+    CUcontext ctx = nullptr;
+    return fn(&ctx) == CUDA_SUCCESS ? ctx : nullptr;
+}
+
 // The device address of g_head_scratch in the current device's context.
 cudaError_t scratch_for_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    CUcontext ctx = nullptr;
-    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lock(g_mu);
     ScratchAddr& s = g_scratch[dev];
     if (!s.ptr || !ctx || ctx != s.ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_head_scratch);
         if (e != cudaSuccess) return e;
-        if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+        ctx = current_context();
         s.ptr = p;
         s.ctx = ctx;
     }

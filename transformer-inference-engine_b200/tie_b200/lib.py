@@ -19,7 +19,7 @@ KV_STATUS = ["KV_OK", "KV_ERR_ARG", "KV_ERR_CAPACITY", "KV_ERR_NOMEM"]
 for _i, _n in enumerate(MODEL_STATUS + KV_STATUS):
     globals()[_n] = _i if _n in MODEL_STATUS else KV_STATUS.index(_n)
 MODEL_PATH_NOCACHE, MODEL_PATH_CACHE = 0, 1
-TIE_STEP_PERSISTENT, TIE_STEP_CHAINED = 0, 1
+TIE_STEP_PERSISTENT, TIE_STEP_CHAINED, TIE_STEP_UNFUSED = 0, 1, 2
 TIE_WEIGHTS_F32, TIE_WEIGHTS_BF16, TIE_WEIGHTS_INT8 = 0, 1, 2
 MODEL_CPROJ_AS_STORED, MODEL_CPROJ_TRANSPOSED = 0, 1
 
@@ -119,6 +119,7 @@ def library():
         "model_generate_greedy_device": (C.c_int, [_vp, _vp, C.c_size_t, C.c_size_t, C.c_size_t, _vp]),
         "model_time_kernel": (C.c_int, [_vp, C.c_int, C.c_size_t, C.c_size_t, C.c_int, _fp]),
         "model_set_step_kernel": (C.c_int, [_vp, C.c_int]),
+        "model_debug_wait_drill": (C.c_int, [_vp, C.c_uint64]),
         "model_set_weight_format": (C.c_int, [_vp, C.c_int]),
         "model_weight_format": (C.c_int, [_vp]),
         "model_step_trace": (C.c_int, [_vp, C.c_size_t, C.c_size_t, _vp, C.c_size_t,
@@ -292,8 +293,14 @@ class Model:
         return library().model_weight_format(self.h)
 
     def set_step_kernel(self, kind):
-        """TIE_STEP_CHAINED (default) or TIE_STEP_PERSISTENT (decode steps of <= 4 sequences)."""
+        """TIE_STEP_CHAINED (default), TIE_STEP_UNFUSED (the same arithmetic as separate
+        kernels) or TIE_STEP_PERSISTENT (decode steps of <= 4 sequences)."""
         _chk(library().model_set_step_kernel(self.h, kind), "model_set_step_kernel")
+
+    def debug_wait_drill(self, limit_ns: int):
+        """The next chained decode step waits on a barrier nothing completes for
+        limit_ns and reports MODEL_ERR_DEVICE (model_debug_wait_drill)."""
+        _chk(library().model_debug_wait_drill(self.h, int(limit_ns)), "model_debug_wait_drill")
 
     def step_trace(self, rows: int, context: int) -> np.ndarray:
         """Global-timer stamps (ns) of one persistent decode step: [n_cta, per_cta]."""
