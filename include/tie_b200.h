@@ -140,19 +140,19 @@ int model_weight_format(const model *m);
 const char *tie_last_device_error(void);
 
 /* ---- how small decode steps run ------------------------------------------
- * A decode step of at most 8 sequences runs as a chain of kernels linked by
- * programmatic dependent launch: TIE_STEP_CHAINED, the default, five per layer
- * (LayerNorm + QKV + the step's K/V rows; attention chunk partials; their
- * merge + attention projection + residual; LayerNorm + FC + GELU; MLP
- * projection + residual), each matmul's weights streamed into shared memory
- * ahead of its dependency wait. TIE_STEP_UNFUSED runs the same arithmetic as
- * separate kernels (LayerNorm, embedding and attention merge on their own, the
- * weights held in registers), seven per layer. With TIE_STEP_PERSISTENT a step
- * of at most 4 sequences (fp32 weights, without attention statistics) runs as
- * ONE persistent kernel instead. All three form every sum in the same order,
- * so they return identical logits and tokens; the switch exists to compare
- * and time them. MODEL_ERR_ARG for any other value. */
-enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1, TIE_STEP_UNFUSED = 2 };
+ * A decode step of at most 8 sequences runs as a chain of per-layer kernels
+ * linked by programmatic dependent launch: TIE_STEP_CHAINED, the default
+ * (LayerNorm, QKV + the step's K/V rows, attention, projection + residual,
+ * LayerNorm, FC + GELU, MLP projection + residual; each matmul's weights are
+ * loaded into registers ahead of its dependency wait). TIE_STEP_STREAM runs
+ * the same arithmetic as five kernels per layer: the weights are bulk-copied
+ * into shared memory ahead of the wait, and LayerNorm, the embedding lookup
+ * and the merge of attention chunk partials run in the matmuls' prologues. With
+ * TIE_STEP_PERSISTENT a step of at most 4 sequences (fp32 weights, without
+ * attention statistics) runs as ONE persistent kernel. All three form every
+ * sum in the same order, so they return identical logits and tokens; the
+ * switch exists to compare and time them. MODEL_ERR_ARG for any other value. */
+enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1, TIE_STEP_STREAM = 2 };
 
 /* Failure drill for the bounded waits: the next decode step that runs on the
  * default chained path (at most 8 sequences, no attention statistics) has its
@@ -164,6 +164,19 @@ enum { TIE_STEP_PERSISTENT = 0, TIE_STEP_CHAINED = 1, TIE_STEP_UNFUSED = 2 };
  * same flag. MODEL_ERR_ARG for a NULL model or a zero limit. No counterpart in
  * the reference (its CPU engine has no device waits). */
 model_status model_debug_wait_drill(model *m, uint64_t limit_ns);
+
+/* Trace of one decode step of `rows` (<= 8) sequences at context `context` on
+ * the TIE_STEP_STREAM path (the batch pool must cover them; contents are
+ * overwritten as for model_time_kernel): for each of its 4 * n_layer + 1
+ * streaming matmul kernels in launch order, *per_kernel global-timer stamps
+ * (ns) -- 256 CTA slots of 8 events: entry, dependency wait over, input rows
+ * built, first weights landed, last stage done, exit, producer done (0 where
+ * no CTA ran) -- written to out (host, cap >= *per_kernel * *n_kernels;
+ * *per_kernel and *n_kernels are set even when the capacity is short, which
+ * returns MODEL_ERR_CAPACITY). MODEL_ERR_ARG when the step would not take that
+ * path. No counterpart in the reference. */
+model_status model_stream_trace(model *m, size_t rows, size_t context, uint64_t *out, size_t cap,
+                                size_t *per_kernel, size_t *n_kernels);
 model_status model_set_step_kernel(model *m, int kind);
 
 /* Trace of one persistent decode step of `rows` (<= 4) sequences at context

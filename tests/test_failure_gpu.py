@@ -1,7 +1,8 @@
 """Failure detection on the GPU without a fault: a bounded wait that runs out.
 
-model_debug_wait_drill makes the next decode step's first matmul wait on a
-shared-memory barrier that nothing completes. The wait gives up after the
+model_debug_wait_drill makes the next decode step's first matmul (on the
+TIE_STEP_STREAM path, whose kernels wait on shared-memory barriers for their
+bulk copies) wait on a barrier that nothing completes. The wait gives up after the
 given limit, the kernel records the expiry in the model's device error flag
 and returns; the call must report MODEL_ERR_DEVICE, leave the cache length
 where it was, and the next step must run normally -- bit-identical to a model
@@ -17,6 +18,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _steps(m, prompts, n, drill_at=None):
+    m.set_step_kernel(tie_b200.TIE_STEP_STREAM)
     S, T = prompts.shape
     m.batch_reserve(S, T + n + 2)
     nxt, _ = m.prefill_batch(prompts)

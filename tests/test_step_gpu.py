@@ -111,14 +111,14 @@ def test_chained_is_the_default():
 @pytest.mark.parametrize("shape", ["tiny", "mini", "small"])
 @pytest.mark.parametrize("n_seq", [1, 2, 3, 5, 8])
 def test_stream_chain_bit_identical_to_unfused(shape, n_seq):
-    """The default chain (weights streamed into shared memory, LayerNorm,
+    """The stream chain (weights streamed into shared memory, LayerNorm,
     embedding and the attention merge folded into the matmuls) against the
-    same arithmetic as separate kernels: identical logits and tokens."""
+    default chain of separate kernels: identical logits and tokens."""
     with _model(shape) as m:
         prompts = synth.prompt_ids(m.vocab, n_seq, 19, seed=70 + n_seq)
         n_steps = 36 if shape != "small" else 12
-        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, n_steps)
-        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_UNFUSED, prompts, n_steps)
+        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_STREAM, prompts, n_steps)
+        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, n_steps)
         assert np.array_equal(ts, tu)
         bad = np.argwhere(ls.view(np.uint32) != lu.view(np.uint32))
         assert len(bad) == 0, f"{len(bad)} logits differ, first {bad[:3].tolist()}"
@@ -130,8 +130,8 @@ def test_stream_chain_reduced_formats_bit_identical(fmt, n_seq):
     with _model("mini") as m:
         m.set_weight_format(fmt)
         prompts = synth.prompt_ids(m.vocab, n_seq, 23, seed=80 + n_seq)
-        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, 20)
-        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_UNFUSED, prompts, 20)
+        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_STREAM, prompts, 20)
+        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, 20)
         assert np.array_equal(ts, tu)
         assert np.array_equal(ls.view(np.uint32), lu.view(np.uint32))
 
@@ -140,7 +140,7 @@ def test_stream_chain_long_context_bit_identical():
     """Past 256 positions the merge folds more than 16 chunk partials."""
     with _model("small", seed=1234, ln="unit") as m:
         prompts = synth.prompt_ids(m.vocab, 2, 700, seed=93)
-        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, 4)
-        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_UNFUSED, prompts, 4)
+        ls, ts = _decode_trace(m, tie_b200.TIE_STEP_STREAM, prompts, 4)
+        lu, tu = _decode_trace(m, tie_b200.TIE_STEP_CHAINED, prompts, 4)
         assert np.array_equal(ts, tu)
         assert np.array_equal(ls.view(np.uint32), lu.view(np.uint32))

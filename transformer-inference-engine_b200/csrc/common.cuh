@@ -263,7 +263,12 @@ struct StreamParams {
     int* err;                     // set when a bounded wait expires
     int stall;                    // failure drill: wait on a barrier nothing completes
     unsigned long long wait_ns;   // the bounded waits' limit (0: one second)
+    unsigned long long* trace;    // NULL, or [grid][kStreamTraceEvents] global-timer stamps per CTA
 };
+// Stream-kernel trace, per CTA (global-timer ns): 0 entry, 1 dependency wait
+// over, 2 input rows built, 3 first stage's weights landed, 4 last stage
+// finished, 5 exit, 6 the producer issued its last copy.
+constexpr int kStreamTraceEvents = 8;
 // Whether every matmul of a decode step of M rows of a model of width E (and
 // MLP width 4E) runs on the stream path; the choice depends on M and E only.
 bool stream_applies(int M, int E, int wt);

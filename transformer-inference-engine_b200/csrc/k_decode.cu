@@ -455,9 +455,10 @@ int head_blocks_wt(int V, int K, int M) {
 constexpr int kSgCompute = 8;                       // compute warps
 constexpr int kSgThreads = (kSgCompute + 1) * 32;   // + the producer warp
 constexpr int kSgMaxRows = 8;                       // activation rows
-constexpr int kSgMaxStages = 4;
+constexpr int kSgMaxStages = 8;
 constexpr int kSgStageTarget = 24 * 1024;           // bytes of weights per stage, about
-constexpr int kSgSmemBudget = 110 * 1024;           // two consecutive kernels' CTAs share an SM
+constexpr int kSgSmemBudget = 100 * 1024;           // two consecutive kernels' CTAs share an SM
+constexpr int kSgHeadBudget = 200 * 1024;           // the head, last in the chain, takes the SM
 constexpr int kSgXsMax = 48 * 1024;                 // input rows staged in shared memory up to this size
 constexpr int kAttnD = 64, kAttnPart = kAttnD + 2, kAttnPg = 16;
 
@@ -490,16 +491,17 @@ struct SgArgs {
     int* err;
     int stall;
     unsigned long long wait_ns;
+    unsigned long long* trace;
 };
 
 // fixed part of the shared-memory layout: barriers, reductions, partial sums,
 // per-row epilogue operands; then x rows, then the ring
 struct SgFixed {
-    static constexpr uint32_t bars = 0;                                   // full[4], empty[4], never, flags
-    static constexpr uint32_t red = 128;                                  // double [2][8 rows][8 groups]
+    static constexpr uint32_t bars = 0;                                   // full[8], empty[8], never, flag
+    static constexpr uint32_t red = 256;                                  // double [2][8 rows][8 groups]
     static constexpr uint32_t part = red + 2 * kSgMaxRows * 8 * 8;        // float [2][8 warps][8 rows]
-    static constexpr uint32_t best = part + 2 * kSgCompute * kSgMaxRows * 4;  // (float, int) [64]
-    static constexpr uint32_t lens = best + 64 * 8;                       // int [8]
+    static constexpr uint32_t best = part + 2 * kSgCompute * kSgMaxRows * 4;  // (float, int) [16 warps][8]
+    static constexpr uint32_t lens = best + kSgCompute * kSgMaxRows * 8;  // int [8]
     static constexpr uint32_t epi = lens + kSgMaxRows * 4;                // bias [R], scale [R], resid [M][R]
 };
 
@@ -526,16 +528,12 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(sg_smem + SgFixed::bars);
     uint64_t* empty = full + kSgMaxStages;
     uint64_t* never = empty + kSgMaxStages;
-    // stop: any warp gave up (producer or compute). quit[i & 1]: a compute warp
-    // gave up in stage i; it is set only before stage i's compute barrier and
-    // read only after it (never cleared), so every compute warp reads the same
-    // value and they leave the stage loop together
+    // set once any warp gives up a bounded wait; the others then stop waiting
     volatile int* stop = reinterpret_cast<volatile int*>(never + 1);
-    volatile int* quit = stop + 1;
     double* s_red = reinterpret_cast<double*>(sg_smem + SgFixed::red);
     float* s_part = reinterpret_cast<float*>(sg_smem + SgFixed::part);
     float* s_bv = reinterpret_cast<float*>(sg_smem + SgFixed::best);
-    int* s_bi = reinterpret_cast<int*>(sg_smem + SgFixed::best + 64 * 4);
+    int* s_bi = reinterpret_cast<int*>(sg_smem + SgFixed::best + kSgCompute * kSgMaxRows * 4);
     int* s_lens = reinterpret_cast<int*>(sg_smem + SgFixed::lens);
     const int R = a.gpc * a.g;   // weight rows of this CTA's range
     float* s_bias = reinterpret_cast<float*>(sg_smem + SgFixed::epi);
@@ -553,6 +551,8 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
     const int ng = max(0, min(a.gpc, (a.N + a.g - 1) / a.g - g0));      // groups of this CTA
     const int row_base = g0 * a.g;
     const unsigned long long limit = a.wait_ns ? a.wait_ns : kWaitNs;
+    unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * kStreamTraceEvents : nullptr;
+    if (tr && tid == 0) tr[0] = gtime();
 
     if (tid == 0) {
         for (int s = 0; s < kSgMaxStages; ++s) {
@@ -561,8 +561,6 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
         }
         mbar_init(never, 1);
         *stop = 0;
-        quit[0] = 0;
-        quit[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -587,6 +585,7 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
                 bulk_load(ring + (size_t)slot * a.stage_bytes, a.W + (size_t)row0 * row_bytes, bytes, &full[slot], pol);
                 ++issued;
             }
+            if (tr) tr[6] = gtime();
             // every copy this thread started has landed before the CTA may exit
             for (int j = issued > S ? issued - S : 0; j < issued; ++j)
                 if (!sg_wait(&full[j % S], (uint32_t)(j / S) & 1u, limit, stop)) {
@@ -608,8 +607,8 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
         for (int t = tid; t < R; t += kSgCompute * 32)
             s_scale[t] = row_base + t < a.N ? __ldg(a.scale + row_base + t) : 1.f;
     }
-    float gam[8], bet[8];   // LayerNorm gain and shift of elements tid + 256 j
-    if (PRO == STREAM_PRO_LN || PRO == STREAM_PRO_EMBED_LN) {
+    float gam[8], bet[8];   // LayerNorm gain and shift of elements tid + 256 j (threads < 256)
+    if ((PRO == STREAM_PRO_LN || PRO == STREAM_PRO_EMBED_LN) && tid < 256) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int i = tid + 256 * j;
@@ -618,6 +617,7 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
         }
     }
     pdl_wait();
+    if (tr && tid == 0) tr[1] = gtime();
 
     // ----------------------------------------------------------- prologue
     if (tid < M && (PRO == STREAM_PRO_EMBED_LN || PRO == STREAM_PRO_MERGE || EPI == DEC_QKV_KV))
@@ -657,15 +657,17 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
         // LayerNorm of every row in place, the canonical order: thread tid is
         // virtual lane tid, warp w group w
         bar_sync(1, kSgCompute * 32);
+        // the canonical sums are formed by threads 0..255 (virtual lanes), warps 0..7 (groups)
+        const bool vl = tid < 256;
         double acc[MB];
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
             acc[m] = 0.0;
-            if (m < M)
+            if (m < M && vl)
                 for (int i = tid; i < K; i += 256) acc[m] = __dadd_rn(acc[m], (double)x_s[m * K + i]);
             acc[m] = ln_warp_sum_d(acc[m]);
         }
-        if (lane == 0)
+        if (lane == 0 && vl)
 #pragma unroll
             for (int m = 0; m < MB; ++m) s_red[m * 8 + warp] = acc[m];
         bar_sync(1, kSgCompute * 32);
@@ -677,14 +679,14 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
             for (int w = 1; w < kLnGroups; ++w) S_ = __dadd_rn(S_, s_red[m * 8 + w]);
             mean[m] = S_ / (double)K;
             acc[m] = 0.0;
-            if (m < M)
+            if (m < M && vl)
                 for (int i = tid; i < K; i += 256) {
                     const double d = __dadd_rn((double)x_s[m * K + i], -mean[m]);
                     acc[m] = __dadd_rn(acc[m], __dmul_rn(d, d));
                 }
             acc[m] = ln_warp_sum_d(acc[m]);
         }
-        if (lane == 0)
+        if (lane == 0 && vl)
 #pragma unroll
             for (int m = 0; m < MB; ++m) s_red[kSgMaxRows * 8 + m * 8 + warp] = acc[m];
         bar_sync(1, kSgCompute * 32);
@@ -695,11 +697,12 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
 #pragma unroll
             for (int w = 1; w < kLnGroups; ++w) V_ = __dadd_rn(V_, s_red[kSgMaxRows * 8 + m * 8 + w]);
             const float inv = (float)(1.0 / sqrt(__dadd_rn(V_ / (double)K, (double)a.eps)));
+            if (vl)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = tid + 256 * j;
-                if (i < K) x_s[m * K + i] = ln_apply(x_s[m * K + i], mean[m], inv, gam[j], bet[j]);
-            }
+                for (int j = 0; j < 8; ++j) {
+                    const int i = tid + 256 * j;
+                    if (i < K) x_s[m * K + i] = ln_apply(x_s[m * K + i], mean[m], inv, gam[j], bet[j]);
+                }
         }
     }
     if (PRO == STREAM_PRO_MERGE) {
@@ -715,16 +718,16 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             float lt = 0.f, o0 = 0.f, o1 = 0.f;
-            for (int k0 = 0; k0 < ns; k0 += 8) {
-                float2 ml[8], ov[8];
+            for (int k0 = 0; k0 < ns; k0 += 16) {
+                float2 ml[16], ov[16];
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
+                for (int k = 0; k < 16; ++k)
                     if (k0 + k < ns) {
                         ml[k] = __ldcg(reinterpret_cast<const float2*>(P + (size_t)(k0 + k) * kAttnPart));
                         ov[k] = __ldcg(reinterpret_cast<const float2*>(P + (size_t)(k0 + k) * kAttnPart + 2 + 2 * lane));
                     }
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
+                for (int k = 0; k < 16; ++k)
                     if (k0 + k < ns) {
                         const float cf = expf(ml[k].x - mx);
                         lt = fmaf(ml[k].y, cf, lt);
@@ -736,28 +739,33 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
         }
     }
     bar_sync(1, kSgCompute * 32);
+    if (tr && tid == 0) tr[2] = gtime();
 
     // failure drill: a barrier that nothing completes; the bounded wait expires
     if (a.stall && !sg_wait(never, 0, limit, stop)) {
         if (tid == 0) atomicExch(a.err, 1);
-        quit[0] = 1;
         *stop = 1;
     }
 
     // -------------------------------------------------------------- stages
+    // Warps run through the stages independently (a warp that gives up keeps
+    // going without computing, so every barrier below is met by all of its
+    // warps). With WS = 1 a warp owns a whole row and finishes it itself;
+    // with WS = 4 the four warps of a row meet on a 128-thread barrier and the
+    // slice-0 warp adds the slice sums in order.
     const int K4c = K / EPC;                              // 16-byte chunks per row
     const int slice = (K4c + a.ws - 1) / a.ws;
     const int my_r = warp / a.ws, my_s = warp % a.ws;
     const int c0 = my_s * slice, c1 = min(K4c, c0 + slice);
-    float bv = 0.f;   // head: this thread's best (value, index) and the NaN-at-0 flag
+    float bv = 0.f;   // head: this lane's best (value, index) for activation row `lane`, and NaN at 0
     int bi = -1;
     bool nan0 = false;
     for (int i = 0; i < ng; ++i) {
         const int slot = i % S, buf = i & 1;
         const int row0 = (g0 + i) * a.g, rows = min(a.g, a.N - row0);
         const bool ok = sg_wait(&full[slot], (uint32_t)(i / S) & 1u, limit, stop);
+        if (tr && tid == 0 && i == 0) tr[3] = gtime();
         if (!ok) {
-            quit[buf] = 1;
             *stop = 1;
             if (lane == 0) atomicExch(a.err, 1);
         }
@@ -787,6 +795,8 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
                 }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);   // the ring slot is read
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
             float v = acc[m];
@@ -794,18 +804,24 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             acc[m] = v;
         }
-        if (lane == 0)
+        // lane m's value for activation row m
+        float mine = acc[0];
 #pragma unroll
-            for (int m = 0; m < MB; ++m) s_part[(buf * kSgCompute + warp) * kSgMaxRows + m] = acc[m];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        bar_sync(1, kSgCompute * 32);
-        if (quit[buf]) break;
-        // epilogue: thread t finishes (row t / M, activation row t % M)
-        if (tid < rows * M) {
-            const int rr = tid / M, m = tid % M, j = row0 + rr, lr = i * a.g + rr;
-            float sum = s_part[(buf * kSgCompute + rr * a.ws) * kSgMaxRows + m];
-            for (int k = 1; k < a.ws; ++k) sum += s_part[(buf * kSgCompute + rr * a.ws + k) * kSgMaxRows + m];
+        for (int m = 1; m < MB; ++m)
+            if (lane == m) mine = acc[m];
+        bool fin = my_r < rows && lane < M;   // this lane finishes (row my_r, activation row lane)
+        if (a.ws > 1) {
+            if (lane < M) s_part[(buf * kSgCompute + warp) * kSgMaxRows + lane] = mine;
+            bar_sync(2 + my_r, 32 * a.ws);
+            if (my_s != 0) fin = false;
+            else if (fin) {
+                mine = s_part[(buf * kSgCompute + warp) * kSgMaxRows + lane];
+                for (int k = 1; k < a.ws; ++k) mine += s_part[(buf * kSgCompute + warp + k) * kSgMaxRows + lane];
+            }
+        }
+        if (fin && ok) {
+            const int m = lane, j = row0 + my_r, lr = i * a.g + my_r;
+            float sum = mine;
             if constexpr (WT == 2) sum = sum * s_scale[lr];
             if (EPI == DEC_HEAD) {
                 if (a.y) a.y[(size_t)m * a.ldy + j] = sum;
@@ -827,19 +843,20 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
             }
         }
     }
+    if (tr && tid == 0) tr[4] = gtime();
     if (EPI == DEC_HEAD) {
-        // this CTA's best per activation row: the g threads of a row, in order
-        const int nthr = a.g * M;
-        if (tid < nthr) {
-            s_bv[tid] = bv;
-            s_bi[tid] = nan0 ? -2 : bi;
+        // this CTA's best per activation row over the warps' bests
+        if (lane < kSgMaxRows) {
+            s_bv[warp * kSgMaxRows + lane] = bv;
+            s_bi[warp * kSgMaxRows + lane] = nan0 ? -2 : bi;
         }
         bar_sync(1, kSgCompute * 32);
         if (tid < M) {
             float b2 = 0.f;
             int i2 = -1;
             bool n2 = false;
-            for (int t = tid; t < nthr; t += M) {
+            for (int w = 0; w < kSgCompute; ++w) {
+                const int t = w * kSgMaxRows + tid;
                 if (s_bi[t] == -2) n2 = true;
                 else if (s_bi[t] >= 0 && beats(s_bv[t], s_bi[t], b2, i2)) { b2 = s_bv[t]; i2 = s_bi[t]; }
             }
@@ -847,6 +864,7 @@ stream_gemv_kernel(const __grid_constant__ SgArgs a) {
             a.part_idx[(size_t)blockIdx.x * M + tid] = n2 ? -2 : i2;
         }
     }
+    if (tr && tid == 0) tr[5] = gtime();
 }
 
 }  // namespace
@@ -902,7 +920,7 @@ bool sg_geometry(int M, int N, int K, int wt, int pro, int epi, bool head, SgGeo
     o->off_x = sg_align(SgFixed::epi + epi_span, 128);
     o->off_ring = sg_align(o->off_x + (xs ? xbytes : 0), 128);
     o->stage_bytes = sg_align((uint32_t)(g * row_bytes), 128);
-    const int budget = kSgSmemBudget - (int)o->off_ring;
+    const int budget = (head ? kSgHeadBudget : kSgSmemBudget) - (int)o->off_ring;
     o->stages = std::min({kSgMaxStages, gpc, budget / (int)o->stage_bytes});
     if (o->stages < 1) return false;
     o->smem = o->off_ring + (uint32_t)o->stages * o->stage_bytes;
@@ -914,7 +932,10 @@ cudaError_t sg_launch(const SgArgs& a, const SgGeom& g, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(stream_gemv_kernel<WT, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSgSmemBudget);
+                                             kSgHeadBudget);
+        if (e != cudaSuccess) return e;
+        // the whole unified array as shared memory: two CTAs of consecutive kernels fit
+        e = cudaFuncSetAttribute(stream_gemv_kernel<WT, MB>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
         configured = true;
     }
@@ -974,7 +995,7 @@ cudaError_t launch_stream_gemv(const StreamParams& p, cudaStream_t st) {
     a.part_val = p.part_val; a.part_idx = p.part_idx;
     a.g = g.g; a.ws = g.ws; a.stages = g.stages; a.gpc = g.gpc; a.xs = g.xs;
     a.stage_bytes = g.stage_bytes; a.off_x = g.off_x; a.off_ring = g.off_ring;
-    a.err = p.err; a.stall = p.stall; a.wait_ns = p.wait_ns;
+    a.err = p.err; a.stall = p.stall; a.wait_ns = p.wait_ns; a.trace = p.trace;
     if (p.wt == 1) return sg_launch_m<1>(a, g, st);
     if (p.wt == 2) return sg_launch_m<2>(a, g, st);
     return sg_launch_m<0>(a, g, st);

@@ -152,6 +152,9 @@ struct Mat {
 // the tensor cores.
 constexpr int kGemvRows = 8;
 
+// CTAs a stream-kernel trace reserves per kernel (at most one per SM)
+constexpr int kTraceCtas = 256;
+
 // One instantiated decode graph per (batch size, cache, advance, output) key,
 // with the number of kernels one replay runs.
 struct GraphKey {
@@ -245,6 +248,10 @@ struct model {
     // failure drill: the next decode step's first matmul waits on a barrier
     // nothing completes, for at most drill_ns (model_debug_wait_drill)
     unsigned long long drill_ns = 0;
+    // stream-kernel trace of one step (model_stream_trace): per stream kernel
+    // in launch order, [grid][kStreamTraceEvents] stamps; NULL otherwise
+    unsigned long long* stream_trace = nullptr;
+    int stream_traced = 0;
 };
 
 namespace {
@@ -550,7 +557,7 @@ model_status build_weight_set(model* m, int fmt) {
 // the matmuls' prologues, every matmul's weights in flight before its
 // dependency wait.                                           model.c:794-868
 bool use_stream(const model* m, int B) {
-    return !m->stats_on && m->step_kind != TIE_STEP_UNFUSED && B <= kGemvRows &&
+    return !m->stats_on && m->step_kind == TIE_STEP_STREAM && B <= kGemvRows &&
            stream_applies(B, m->cfg.n_embd, m->wfmt);
 }
 
@@ -576,6 +583,11 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
     cudaStream_t st = m->st;
     const int max_chunks = attn_decode_max_splits(cache->capacity);
     const StreamParams base = stream_base(m, B);
+    int traced = 0;   // stream kernels launched so far (their trace slot)
+    auto slot = [&](StreamParams& q) {
+        if (m->stream_trace) q.trace = m->stream_trace + (size_t)traced * kTraceCtas * kStreamTraceEvents;
+        ++traced;
+    };
     for (int l = 0; l < m->cfg.n_layer; ++l) {
         const Layer& w = m->layers[l];
         const PagedKV view = layer_view(cache, l);
@@ -588,6 +600,7 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
         stream_weights(p, w.qkv_w, qmat(m, l, 0), w.qkv_b);
         p.y = m->qkv; p.ldy = 3 * E; p.N = 3 * E; p.K = E; p.kv = view;
         if (l == 0 && m->drill_ns) { p.stall = 1; p.wait_ns = m->drill_ns; }
+        slot(p);
         LAUNCH(launch_stream_gemv(p, st));
         // attention: chunk partials
         LAUNCH(launch_attn_chunks(m->qkv, m->d_lens, B, H, view, max_chunks, m->d_part, st));
@@ -598,6 +611,7 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
         p.apart = m->d_part; p.H = H; p.max_chunks = max_chunks;
         stream_weights(p, w.proj_w, qmat(m, l, 1), w.proj_b);
         p.y = m->x; p.ldy = E; p.N = E; p.K = E;
+        slot(p);
         LAUNCH(launch_stream_gemv(p, st));
         // LayerNorm 2 + FC + GELU
         p = base;
@@ -606,6 +620,7 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
         p.x = m->x; p.ldx = E; p.ln_g = w.ln2_w; p.ln_b = w.ln2_b;
         stream_weights(p, w.fc_w, qmat(m, l, 2), w.fc_b);
         p.y = m->ff; p.ldy = 4 * E; p.N = 4 * E; p.K = E;
+        slot(p);
         LAUNCH(launch_stream_gemv(p, st));
         // MLP projection + residual
         p = base;
@@ -614,6 +629,7 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
         p.x = m->ff; p.ldx = 4 * E;
         stream_weights(p, w.mlp_w, qmat(m, l, 3), w.mlp_b);
         p.y = m->x; p.ldy = E; p.N = E; p.K = 4 * E;
+        slot(p);
         LAUNCH(launch_stream_gemv(p, st));
     }
     // LayerNorm f + the tied head with per-CTA greedy partials
@@ -625,9 +641,11 @@ model_status run_decode_stream(model* m, int B, kv_cache* cache, bool advance, i
     stream_weights(p, m->wte, qh, nullptr);
     p.y = m->logits; p.ldy = V; p.N = V; p.K = E;
     p.part_val = m->d_am_val; p.part_idx = m->d_am_idx;
+    slot(p);
     LAUNCH(launch_stream_gemv(p, st));
     LAUNCH(launch_argmax_finalize(m->d_am_val, m->d_am_idx, stream_head_blocks(V, E, qh.wt, B), B, m->d_next, st));
     if (advance) LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, out, ld_out, m->d_step, B, st));
+    m->stream_traced = traced;
     return MODEL_OK;
 }
 
@@ -1603,6 +1621,37 @@ model_status model_set_weight_format(model* m, int fmt) {
 
 int model_weight_format(const model* m) { return m ? m->wfmt : -1; }
 
+model_status model_stream_trace(model* m, size_t rows, size_t context, uint64_t* out, size_t cap,
+                                size_t* per_kernel, size_t* n_kernels) {
+    if (!m || !per_kernel || !n_kernels || rows == 0 || rows > (size_t)kGemvRows || context == 0) return MODEL_ERR_ARG;
+    if (!m->pool || (int)rows > m->pool->n_seq || (int)context > m->pool->capacity) return MODEL_ERR_CAPACITY;
+    if (!use_stream(m, (int)rows)) return MODEL_ERR_ARG;
+    const size_t kernels = 4 * (size_t)m->cfg.n_layer + 1, per = (size_t)kTraceCtas * kStreamTraceEvents;
+    *per_kernel = per;
+    *n_kernels = kernels;
+    if (!out || cap < per * kernels) return MODEL_ERR_CAPACITY;
+    model_status rc = ensure_slots(m, rows, m->pool->capacity);
+    if (rc != MODEL_OK) return rc;
+    std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
+    if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    unsigned long long* d = nullptr;
+    CU(cudaMalloc(&d, per * kernels * sizeof(unsigned long long)));
+    CU(cudaMemsetAsync(d, 0, per * kernels * sizeof(unsigned long long), m->st));
+    rc = run_decode_stream(m, (int)rows, m->pool, false, nullptr, 0);   // warm
+    if (rc == MODEL_OK) {
+        m->stream_trace = d;
+        rc = run_decode_stream(m, (int)rows, m->pool, false, nullptr, 0);
+        m->stream_trace = nullptr;
+    }
+    if (rc == MODEL_OK && cudaMemcpyAsync(out, d, per * kernels * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                                          m->st) != cudaSuccess)
+        rc = MODEL_ERR_DEVICE;
+    if (rc == MODEL_OK) rc = finish(m);
+    cudaStreamSynchronize(m->st);
+    cudaFree(d);
+    return rc;
+}
+
 model_status model_debug_wait_drill(model* m, uint64_t limit_ns) {
     if (!m || limit_ns == 0) return MODEL_ERR_ARG;
     m->drill_ns = limit_ns;
@@ -1610,7 +1659,7 @@ model_status model_debug_wait_drill(model* m, uint64_t limit_ns) {
 }
 
 model_status model_set_step_kernel(model* m, int kind) {
-    if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED && kind != TIE_STEP_UNFUSED))
+    if (!m || (kind != TIE_STEP_PERSISTENT && kind != TIE_STEP_CHAINED && kind != TIE_STEP_STREAM))
         return MODEL_ERR_ARG;
     if (kind != m->step_kind) drop_graphs(m);
     m->step_kind = kind;

@@ -19,7 +19,7 @@ KV_STATUS = ["KV_OK", "KV_ERR_ARG", "KV_ERR_CAPACITY", "KV_ERR_NOMEM"]
 for _i, _n in enumerate(MODEL_STATUS + KV_STATUS):
     globals()[_n] = _i if _n in MODEL_STATUS else KV_STATUS.index(_n)
 MODEL_PATH_NOCACHE, MODEL_PATH_CACHE = 0, 1
-TIE_STEP_PERSISTENT, TIE_STEP_CHAINED, TIE_STEP_UNFUSED = 0, 1, 2
+TIE_STEP_PERSISTENT, TIE_STEP_CHAINED, TIE_STEP_STREAM = 0, 1, 2
 TIE_WEIGHTS_F32, TIE_WEIGHTS_BF16, TIE_WEIGHTS_INT8 = 0, 1, 2
 MODEL_CPROJ_AS_STORED, MODEL_CPROJ_TRANSPOSED = 0, 1
 
@@ -120,6 +120,7 @@ def library():
         "model_time_kernel": (C.c_int, [_vp, C.c_int, C.c_size_t, C.c_size_t, C.c_int, _fp]),
         "model_set_step_kernel": (C.c_int, [_vp, C.c_int]),
         "model_debug_wait_drill": (C.c_int, [_vp, C.c_uint64]),
+        "model_stream_trace": (C.c_int, [_vp, C.c_size_t, C.c_size_t, _vp, C.c_size_t, _vp, _vp]),
         "model_set_weight_format": (C.c_int, [_vp, C.c_int]),
         "model_weight_format": (C.c_int, [_vp]),
         "model_step_trace": (C.c_int, [_vp, C.c_size_t, C.c_size_t, _vp, C.c_size_t,
@@ -293,14 +294,25 @@ class Model:
         return library().model_weight_format(self.h)
 
     def set_step_kernel(self, kind):
-        """TIE_STEP_CHAINED (default), TIE_STEP_UNFUSED (the same arithmetic as separate
-        kernels) or TIE_STEP_PERSISTENT (decode steps of <= 4 sequences)."""
+        """TIE_STEP_CHAINED (default), TIE_STEP_STREAM (the same arithmetic in five
+        kernels per layer, weights streamed through shared memory) or
+        TIE_STEP_PERSISTENT (decode steps of <= 4 sequences)."""
         _chk(library().model_set_step_kernel(self.h, kind), "model_set_step_kernel")
 
     def debug_wait_drill(self, limit_ns: int):
-        """The next chained decode step waits on a barrier nothing completes for
-        limit_ns and reports MODEL_ERR_DEVICE (model_debug_wait_drill)."""
+        """The next TIE_STEP_STREAM decode step waits on a barrier nothing completes
+        for limit_ns and reports MODEL_ERR_DEVICE (model_debug_wait_drill)."""
         _chk(library().model_debug_wait_drill(self.h, int(limit_ns)), "model_debug_wait_drill")
+
+    def stream_trace(self, rows: int, context: int) -> np.ndarray:
+        """Global-timer stamps (ns) of one chained decode step's streaming
+        matmuls: [kernel][cta][event] (model_stream_trace)."""
+        per, n = C.c_size_t(), C.c_size_t()
+        library().model_stream_trace(self.h, rows, context, None, 0, C.byref(per), C.byref(n))
+        out = np.zeros((n.value, per.value), dtype=np.uint64)
+        _chk(library().model_stream_trace(self.h, rows, context, out.ctypes.data_as(_vp), out.size,
+                                          C.byref(per), C.byref(n)), "model_stream_trace")
+        return out.reshape(n.value, -1, 8)
 
     def step_trace(self, rows: int, context: int) -> np.ndarray:
         """Global-timer stamps (ns) of one persistent decode step: [n_cta, per_cta]."""
