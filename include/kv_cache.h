@@ -14,9 +14,15 @@
  * [capacity, n_embd] block and the reference's addressing (row p at
  * base + p * n_embd) holds exactly.
  *
- * Pointers. kv_cache_keys/values/*_row return DEVICE addresses. The store
- * functions accept host or device source rows (the copy direction is inferred
- * from the pointer). kv_cache_copy_layer_to_host reads a layer back for tests.
+ * Pointers. For a cache made by kv_cache_create, kv_cache_keys/values/*_row
+ * return addresses in CUDA managed memory: the kernels read them on the device,
+ * and a caller may read rows through them on the host between calls (as the
+ * reference's own tests and callers do; the first device access after a host
+ * read migrates the touched pages back). Multi-sequence pools (the batch API)
+ * are plain device memory: their whole-layer and row views are NULL and
+ * kv_cache_write refuses them with KV_ERR_ARG. The store functions accept host
+ * or device source rows (the copy direction is inferred from the pointer).
+ * kv_cache_copy_layer_to_host reads a layer back into a host buffer.
  *
  * Footprint: n_layer * 2 * capacity * n_embd * 4 bytes, computed from the
  * arguments (reference kv_cache.h:20-22).

@@ -31,11 +31,16 @@ REF_INVENTORY_BIN = os.path.join(HERE, "_ref", "st_inventory")
 def build(reference_root: str | None = None) -> None:
     """Compiles liboracle.so, and the reference binaries when the reference
     source tree is present (its location: `reference_root`, else the
-    TIE_REFERENCE_ROOT environment variable, else the Makefile's default)."""
+    TIE_REFERENCE_ROOT environment variable, else the Makefile's default):
+    its CPU engine, and its C callers linked with the engine's library."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
     ref = reference_root or os.environ.get("TIE_REFERENCE_ROOT")
-    cmd = ["make", "-s", "-C", HERE, "ref-if-present"] + ([f"REF={ref}"] if ref else [])
-    subprocess.run(cmd, check=True)
+    extra = [f"REF={ref}"] if ref else []
+    subprocess.run(["make", "-s", "-C", HERE, "ref-if-present"] + extra, check=True)
+    # the reference's own C callers linked with the engine (needs the engine built)
+    engine = os.path.join(os.path.dirname(HERE), "transformer-inference-engine_b200", "lib", "libtie_b200.so")
+    if os.path.isfile(engine):
+        subprocess.run(["make", "-s", "-C", HERE, "callers-if-present"] + extra, check=True)
 
 
 def reference_available() -> bool:

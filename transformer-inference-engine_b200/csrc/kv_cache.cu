@@ -39,7 +39,14 @@ static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, b
     const size_t per = (size_t)n_layer * c->rows * n_embd * sizeof(float);
     std::vector<int> table((size_t)n_seq * c->pages_per_seq);
     for (size_t i = 0; i < table.size(); ++i) table[i] = (int)i;  // pages in order
-    if (cudaMalloc(&c->k, per) != cudaSuccess || cudaMalloc(&c->v, per) != cudaSuccess ||
+    // A one-sequence cache is managed memory: its kv_cache_keys/values/*_row
+    // addresses are usable on the host too (the reference's callers read rows
+    // through them between calls), and its pages live in device memory while
+    // the kernels use them. A pool stays plain device memory.
+    auto alloc = [&](float** p) {
+        return contiguous ? cudaMallocManaged(p, per, cudaMemAttachGlobal) : cudaMalloc(p, per);
+    };
+    if (alloc(&c->k) != cudaSuccess || alloc(&c->v) != cudaSuccess ||
         cudaMalloc(&c->d_page_table, table.size() * sizeof(int)) != cudaSuccess ||
         cudaMemset(c->k, 0, per) != cudaSuccess || cudaMemset(c->v, 0, per) != cudaSuccess ||
         cudaMemcpy(c->d_page_table, table.data(), table.size() * sizeof(int),
