@@ -177,6 +177,7 @@ model_status model_debug_wait_drill(model *m, uint64_t limit_ns);
  * path. No counterpart in the reference. */
 model_status model_stream_trace(model *m, size_t rows, size_t context, uint64_t *out, size_t cap,
                                 size_t *per_kernel, size_t *n_kernels);
+
 model_status model_set_step_kernel(model *m, int kind);
 
 /* Trace of one persistent decode step of `rows` (<= 4) sequences at context

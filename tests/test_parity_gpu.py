@@ -157,6 +157,26 @@ def test_small_config2_prefill_sweep():
             del logits
 
 
+def teacher_forced_topk_error(m, g, fmt=None):
+    """Feeds the reference's own greedy ids through the batch decode API and
+    returns the largest |logit - reference logit| at the reference's top-k
+    indices over every decode step (step k's logits choose ids[k])."""
+    if fmt is not None:
+        m.set_weight_format(fmt)
+    prompts, ids = g["prompts"], g["ids"]
+    S, T = prompts.shape
+    n_new = ids.shape[1]
+    m.batch_reserve(S, T + n_new)
+    m.prefill_batch(prompts)
+    worst = 0.0
+    rows = np.arange(S)[:, None]
+    for k in range(1, n_new):
+        _, lg = m.decode_step_batch(ids[:, k - 1], want_logits=True)
+        got = lg[rows, g["topk_ids"][:, k]]
+        worst = max(worst, float(np.abs(got - g["topk_vals"][:, k]).max()))
+    return worst
+
+
 def test_medium_config3_greedy():
     g, meta = golden("medium_c3")
     s = meta["spec"]
@@ -164,6 +184,9 @@ def test_medium_config3_greedy():
         m.batch_reserve(s["n_seq"], s["n_prompt"] + s["n_new"])
         out = m.generate_greedy(g["prompts"], s["n_new"])
         assert_ids(out, g)
+        worst = teacher_forced_topk_error(m, g)
+        print(f"config 3: worst top-8 logit error over 8 x 255 steps {worst:.3g}")
+        assert worst <= LOGIT_TOL, worst
 
 
 def test_xl_config4_greedy():
@@ -173,6 +196,9 @@ def test_xl_config4_greedy():
         m.batch_reserve(1, s["n_prompt"] + s["n_new"])
         out = m.generate_greedy(g["prompts"], s["n_new"])
         assert_ids(out, g)
+        worst = teacher_forced_topk_error(m, g)
+        print(f"config 4: worst top-8 logit error over 127 steps {worst:.3g}")
+        assert worst <= LOGIT_TOL, worst
 
 
 def test_small_config5_throughput_ids():

@@ -78,6 +78,25 @@ def test_format_error_against_fp32(fmt):
         assert np.array_equal(again, base)
 
 
+# stated error of the formats against the REFERENCE's fp32 logits (its CPU
+# engine on the fp32 weights), teacher-forced along the reference's own greedy
+# ids, at the reference's top-k indices of every decode step
+STATED_VS_REFERENCE = {("small_c1", "bf16"): 0.05, ("small_c1", "int8"): 0.25,
+                       ("xl_c4", "bf16"): 0.1, ("xl_c4", "int8"): 0.5}
+
+
+@pytest.mark.parametrize("fixture", ["small_c1", "xl_c4"])
+@pytest.mark.parametrize("fmt", sorted(FMTS))
+def test_format_error_against_reference_logits(fixture, fmt):
+    from conftest import golden
+    from test_parity_gpu import model_for, teacher_forced_topk_error
+    g, meta = golden(fixture)
+    with model_for(meta) as m:
+        err = teacher_forced_topk_error(m, g, FMTS[fmt])
+        print(f"{fixture} {fmt}: max-abs error vs the reference's fp32 top-k logits {err:.3g}")
+        assert err <= STATED_VS_REFERENCE[(fixture, fmt)], err
+
+
 def test_format_validation():
     with _model("tiny", 7, "random") as m:
         with pytest.raises(tie_b200.ModelError):

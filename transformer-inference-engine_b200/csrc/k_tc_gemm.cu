@@ -603,6 +603,178 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
     }
 }
 
+// ---------------------------------------------------------------------------
+// The tied head of a decode step of 9-256 rows, with the WEIGHTS (the token
+// embedding, [V, E]) as the 128-row MMA operand:
+//
+//   tile: D[128 vocabulary rows n0.., nb activation rows] = W[n0.., :] . X[.., :]^T
+//
+// One MMA per k-step covers every activation row of the step (N = nb, the rows
+// rounded up to 16, at most 256; rows past the batch read zeros from TMA), so
+// each weight element crosses from memory once per step whatever the batch.
+// A CTA owns one tile over the whole of K (no split, so a row's logits do not
+// depend on the batch it decodes in): the 3xTF32 MMAs of tc_gemm_kernel into
+// TMEM, fed by TMA through a deep ring of 128-byte-swizzled k-blocks (32
+// columns), the weight tiles of the first stages requested before
+// griddepcontrol.wait. The epilogue warps read the accumulator back and store
+// it transposed: for each activation row, a warp writes 32 consecutive logits.
+constexpr int kDecStagesMax = 8;
+constexpr int BKD = 32;                    // k-block width: 128-byte rows, 128-byte swizzle
+constexpr uint32_t kDecTileW = BM * 128;   // one k-block of 128 weight rows
+
+__host__ __device__ constexpr uint32_t dec_stage_bytes(int nb) { return 2u * kDecTileW + 2u * (uint32_t)nb * 128u; }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle (layout code 2):
+// rows of 128 bytes (32 tf32) in 8-row, 1024-byte atoms.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    const uint64_t start = (addr >> 4) & 0x3FFFu;
+    const uint64_t lbo = 1;
+    const uint64_t sbo = 1024 >> 4;
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (2ull << 61) /* SW128 */;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
+               const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, TcArgs p,
+               int nb, int S, int tcols) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t SB = dec_stage_bytes(nb);
+    const uint32_t tileX = (uint32_t)nb * 128u;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (uint32_t)S * SB);
+    uint64_t* full = bars;                   // [S]  TMA -> MMA
+    uint64_t* empty = bars + kDecStagesMax;  // [S]  MMA -> TMA
+    uint64_t* tfull = bars + 2 * kDecStagesMax;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kDecStagesMax + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BM;
+    const int nkb = p.K / BKD;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        mbar_init(smem_u32(&tfull[0]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)tcols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+    grid_dep_trigger();
+
+    auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (mbar_try_wait(bar, parity)) return true;
+            if ((i & 255u) == 0) {
+                if (*abort_flag) return false;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
+        }
+        *abort_flag = 1;
+        atomicExch(p.err, 1);
+        return false;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            const int pre = min(S, nkb);
+            // weights first: no earlier kernel writes them
+            for (int kb = 0; kb < pre; ++kb) {
+                const uint32_t base = smem_u32(smem + kb * SB);
+                const uint32_t fb = smem_u32(&full[kb]);
+                mbar_expect_tx(fb, SB);
+                tma_load_2d(base, &tw_hi, fb, kb * BKD, n0);
+                tma_load_2d(base + kDecTileW, &tw_lo, fb, kb * BKD, n0);
+            }
+            grid_dep_wait();
+            for (int kb = 0; kb < pre; ++kb) {
+                const uint32_t base = smem_u32(smem + kb * SB);
+                const uint32_t fb = smem_u32(&full[kb]);
+                tma_load_2d(base + 2 * kDecTileW, &tx_hi, fb, kb * BKD, 0);
+                tma_load_2d(base + 2 * kDecTileW + tileX, &tx_lo, fb, kb * BKD, 0);
+            }
+            int kb = pre;
+            for (; kb < nkb; ++kb) {
+                const int s = kb % S;
+                if (!wait(smem_u32(&empty[s]), ((kb / S) & 1u) ^ 1u)) break;
+                const uint32_t base = smem_u32(smem + s * SB);
+                const uint32_t fb = smem_u32(&full[s]);
+                mbar_expect_tx(fb, SB);
+                tma_load_2d(base, &tw_hi, fb, kb * BKD, n0);
+                tma_load_2d(base + kDecTileW, &tw_lo, fb, kb * BKD, n0);
+                tma_load_2d(base + 2 * kDecTileW, &tx_hi, fb, kb * BKD, 0);
+                tma_load_2d(base + 2 * kDecTileW + tileX, &tx_lo, fb, kb * BKD, 0);
+            }
+            // every copy this thread started has landed before the CTA may exit
+            for (int j = kb > S ? kb - S : 0; j < kb; ++j) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (!mbar_try_wait(smem_u32(&full[j % S]), (j / S) & 1u))
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) { atomicExch(p.err, 1); break; }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(nb >> 3) << 17) |
+                                   ((uint32_t)(BM >> 4) << 24);
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                if (!wait(smem_u32(&full[s]), (kb / S) & 1u)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t base = smem_u32(smem + s * SB);
+#pragma unroll
+                for (int j = 0; j < BKD / 8; ++j) {   // k-steps of 8 tf32 (32 bytes) within the 128-byte rows
+                    const uint64_t w_hi = sw128_desc(base + j * 32);
+                    const uint64_t w_lo = sw128_desc(base + kDecTileW + j * 32);
+                    const uint64_t x_hi = sw128_desc(base + 2 * kDecTileW + j * 32);
+                    const uint64_t x_lo = sw128_desc(base + 2 * kDecTileW + tileX + j * 32);
+                    mma_tf32(tmem, w_lo, x_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    mma_tf32(tmem, w_hi, x_lo, idesc, 1u);
+                    mma_tf32(tmem, w_hi, x_hi, idesc, 1u);
+                }
+                mma_commit(smem_u32(&empty[s]));
+            }
+            // arrives once every MMA of the tile has completed (also when cut short)
+            mma_commit(smem_u32(&tfull[0]));
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const int q = warp & 3;                // TMEM lane quarter: vocabulary rows n0 + q * 32 + lane
+        const bool ok = wait(smem_u32(&tfull[0]), 0);
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const int col = n0 + q * 32 + lane;
+        for (int c = 0; c < nb / 32 + (nb % 32 ? 1 : 0); ++c) {
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+            if (!ok || col >= p.N) continue;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const int row = c * 32 + k;
+                if (row < p.M) p.C[(size_t)row * p.ldc + col] = __uint_as_float(v[k]);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)tcols));
+    }
+}
+
 __global__ void split_hilo_kernel(const float* __restrict__ x, float* __restrict__ hi,
                                   float* __restrict__ lo, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
@@ -629,18 +801,19 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D map over a rows x cols fp32 matrix (row stride ld floats), box BK x box_rows,
-// 64-byte swizzle (the layout sw64_desc describes).
-bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows) {
+// 2-D map over a rows x cols fp32 matrix (row stride ld floats), box box_cols x
+// box_rows: 16 columns with the 64-byte swizzle (the layout sw64_desc
+// describes) or 32 columns with the 128-byte swizzle (sw128_desc).
+bool make_map(CUtensorMap* map, const float* base, int rows, int cols, int ld, int box_rows, int box_cols = BK) {
     auto fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE, box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int num_sms() {
@@ -721,7 +894,38 @@ cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t 
     return launch_split<EPI, OUT>(op, a, splits, st);
 }
 
+// The tied head of a decode step (tc_head_kernel): op.a_* are the activations
+// (a.M rows), op.b_* the weights (a.N rows).
+cudaError_t launch_head(const TcOperands& op, TcArgs a, cudaStream_t st) {
+    const int nb = (a.M + 15) / 16 * 16;
+    if (nb < 16 || nb > 256) return cudaErrorInvalidValue;
+    CUtensorMap m[4];
+    if (!make_map(&m[0], op.b_hi, a.N, a.K, op.ldb, BM, BKD) || !make_map(&m[1], op.b_lo, a.N, a.K, op.ldb, BM, BKD) ||
+        !make_map(&m[2], op.a_hi, a.M, a.K, op.lda, nb, BKD) || !make_map(&m[3], op.a_lo, a.M, a.K, op.lda, nb, BKD))
+        return cudaErrorInvalidValue;
+    // one CTA per SM: a deep ring keeps several stages' copies in flight
+    const uint32_t sb = dec_stage_bytes(nb);
+    const int S = std::max(2, std::min(kDecStagesMax, (int)((196u * 1024) / sb)));
+    const size_t smem = 1024 + (size_t)S * sb + 256;
+    int tcols = 32;
+    while (tcols < nb) tcols <<= 1;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(tc_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaError_t e = launch_pdl(tc_head_kernel, dim3((a.N + BM - 1) / BM), dim3(THREADS), smem, st, m[0], m[1], m[2],
+                               m[3], a, nb, S, tcols);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_tc_head(const TcOperands& op, const TcArgs& a, cudaStream_t st) {
+    if (!tc_gemm_supported(a.M, a.N, a.K, op.lda, op.ldb) || a.M > 256 || a.K % BKD) return cudaErrorInvalidValue;
+    return launch_head(op, a, st);
+}
 
 bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
     return M > 0 && N > 0 && K > 0 && K % BK == 0 && lda % 4 == 0 && ldb % 4 == 0 && encode_fn() != nullptr;

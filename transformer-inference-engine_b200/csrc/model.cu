@@ -152,6 +152,13 @@ struct Mat {
 // the tensor cores.
 constexpr int kGemvRows = 8;
 
+// The tied head of decode steps of 9..kHeadTileRows rows takes tc_head_kernel:
+// one MMA covers every row of the step, the vocabulary rows being the 128-row
+// operand. (The layer matmuls keep the split-K kernel: with only 6-24 output
+// tiles of 128 they need a cross-CTA reduction either way, and measured on
+// B200 at 256 rows the transposed tile's reduction cost more than it saved.)
+constexpr int kHeadTileRows = 256;
+
 // CTAs a stream-kernel trace reserves per kernel (at most one per SM)
 constexpr int kTraceCtas = 256;
 
@@ -398,6 +405,11 @@ model_status matmul(model* m, bool decode, int rows, Mat x, int ldx, Mat w, int 
     a.C = y; a.C_hi = y_hi; a.C_lo = y_lo; a.ldc = ldy;
     a.err = m->d_err;
     const int out = y_hi ? (y ? TC_OUT_F32_HILO : TC_OUT_HILO) : TC_OUT_F32;
+    if (decode && epi == EPI_STORE && out == TC_OUT_F32 && rows <= kHeadTileRows) {
+        // the tied head of a decode step: the vocabulary as the MMA's 128-row operand
+        LAUNCH(launch_tc_head(op, a, st));
+        return MODEL_OK;
+    }
     const int splits = decode ? tc_splits_for(N, K) : 1;
     LAUNCH(launch_tc_gemm(op, a, epi, out, splits, st));
     return MODEL_OK;

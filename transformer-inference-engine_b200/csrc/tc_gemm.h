@@ -44,6 +44,10 @@ __device__ __forceinline__ float tf32_hi(float x) {
 }
 
 bool tc_gemm_supported(int M, int N, int K, int lda, int ldb);
+// The tied head of a decode step over 1-256 activation rows (op.a_*: a.M rows)
+// against a.N vocabulary rows (op.b_*): the weights are the MMA's 128-row
+// operand, each CTA one tile over the whole of K, logits stored to a.C.
+cudaError_t launch_tc_head(const TcOperands& op, const TcArgs& a, cudaStream_t st);
 int tc_splits_for(int N, int K);
 cudaError_t launch_tc_gemm(const TcOperands& op, const TcArgs& a, int epi, int out, int splits,
                            cudaStream_t st);
