@@ -38,6 +38,9 @@ namespace tie {
 namespace {
 
 constexpr int BM = 128, BK = 16;
+// k-block width of the persistent and head kernels: 128-byte rows, 128-byte
+// swizzle (the split kernel keeps BK, 64-byte rows, to fit two CTAs an SM)
+constexpr int BKD = 32;
 constexpr int THREADS = 192;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -88,6 +91,15 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
     const uint64_t lbo = 1;
     const uint64_t sbo = 512 >> 4;
     return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (4ull << 61) /* SW64 */;
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle (layout code 2):
+// rows of 128 bytes (32 tf32) in 8-row, 1024-byte atoms.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    const uint64_t start = (addr >> 4) & 0x3FFFu;
+    const uint64_t lbo = 1;
+    const uint64_t sbo = 1024 >> 4;
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (2ull << 61) /* SW128 */;
 }
 
 // kind::tf32 instruction descriptor: fp32 accumulate, tf32 A and B, both
@@ -142,9 +154,9 @@ constexpr size_t smem_bytes() {
 }
 
 // The persistent kernel's tile is MT x 128 rows by BN columns: A (hi and lo)
-// MT x 128 rows, B BN rows per 16-wide k-block.
+// MT x 128 rows, B BN rows per 32-wide k-block (128-byte rows).
 template <int BN, int MT>
-constexpr uint32_t stage_bytes_mt() { return 2u * MT * BM * 64 + 2u * BN * 64; }
+constexpr uint32_t stage_bytes_mt() { return 2u * MT * BM * 128 + 2u * BN * 128; }
 
 template <int BN, int MT>
 constexpr int stages_mt() { return (int)((192u * 1024) / stage_bytes_mt<BN, MT>()); }
@@ -166,7 +178,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                TcArgs p) {
     constexpr int S = stages_mt<BN, MT>();
     constexpr uint32_t kStage = stage_bytes_mt<BN, MT>();
-    constexpr uint32_t kTileA = MT * BM * 64, kTileB = BN * 64;
+    constexpr uint32_t kTileA = MT * BM * 128, kTileB = BN * 128;
     constexpr uint32_t kAcc = MT * BN;   // TMEM columns of one accumulator buffer
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -182,7 +194,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
     const int tiles_n = (p.N + BN - 1) / BN, tiles_m = (p.M + MT * BM - 1) / (MT * BM);
     const int tiles_mn = tiles_n * tiles_m;
     const int n_tiles = tiles_mn * p.splits;
-    const int kb_total = p.K / BK;
+    const int kb_total = p.K / BKD;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -241,7 +253,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                     const uint32_t base = smem_u32(smem + s * kStage);
                     const uint32_t fb = smem_u32(&full[s]);
                     mbar_expect_tx(fb, kStage);
-                    const int kx = (kb0 + kb) * BK;
+                    const int kx = (kb0 + kb) * BKD;
                     tma_load_2d(base, &ta_hi, fb, kx, m0);
                     tma_load_2d(base + kTileA, &ta_lo, fb, kx, m0);
                     tma_load_2d(base + 2 * kTileA, &tb_hi, fb, kx, n0);
@@ -276,13 +288,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant_
                     asm volatile("tcgen05.fence::after_thread_sync;");
                     const uint32_t base = smem_u32(smem + s * kStage);
 #pragma unroll
-                    for (int j = 0; j < BK / 8; ++j) {  // k-steps of 8 tf32 (32 bytes)
-                        const uint64_t b_hi = sw64_desc(base + 2 * kTileA + j * 32);
-                        const uint64_t b_lo = sw64_desc(base + 2 * kTileA + kTileB + j * 32);
+                    for (int j = 0; j < BKD / 8; ++j) {  // k-steps of 8 tf32 (32 bytes) within the 128-byte rows
+                        const uint64_t b_hi = sw128_desc(base + 2 * kTileA + j * 32);
+                        const uint64_t b_lo = sw128_desc(base + 2 * kTileA + kTileB + j * 32);
 #pragma unroll
                         for (int mh = 0; mh < MT; ++mh) {   // 128-row halves: rows 128 mh.. of the A tiles
-                            const uint64_t a_hi = sw64_desc(base + mh * BM * 64 + j * 32);
-                            const uint64_t a_lo = sw64_desc(base + kTileA + mh * BM * 64 + j * 32);
+                            const uint64_t a_hi = sw128_desc(base + mh * BM * 128 + j * 32);
+                            const uint64_t a_lo = sw128_desc(base + kTileA + mh * BM * 128 + j * 32);
                             const uint32_t d = acc + (uint32_t)(mh * BN);
                             mma_tf32(d, a_lo, b_hi, idesc, (kb > 0 || j > 0) ? 1u : 0u);
                             mma_tf32(d, a_hi, b_lo, idesc, 1u);
@@ -619,19 +631,9 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
 // griddepcontrol.wait. The epilogue warps read the accumulator back and store
 // it transposed: for each activation row, a warp writes 32 consecutive logits.
 constexpr int kDecStagesMax = 8;
-constexpr int BKD = 32;                    // k-block width: 128-byte rows, 128-byte swizzle
 constexpr uint32_t kDecTileW = BM * 128;   // one k-block of 128 weight rows
 
 __host__ __device__ constexpr uint32_t dec_stage_bytes(int nb) { return 2u * kDecTileW + 2u * (uint32_t)nb * 128u; }
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle (layout code 2):
-// rows of 128 bytes (32 tf32) in 8-row, 1024-byte atoms.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    const uint64_t start = (addr >> 4) & 0x3FFFu;
-    const uint64_t lbo = 1;
-    const uint64_t sbo = 1024 >> 4;
-    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version */ | (2ull << 61) /* SW128 */;
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
 tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
@@ -829,8 +831,9 @@ int num_sms() {
 template <int BN, int MT, int EPI, int OUT>
 cudaError_t launch_bn(const TcOperands& op, const TcArgs& a, int splits, cudaStream_t st) {
     CUtensorMap m[4];
-    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, MT * BM) || !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, MT * BM) ||
-        !make_map(&m[2], op.b_hi, a.N, a.K, op.ldb, BN) || !make_map(&m[3], op.b_lo, a.N, a.K, op.ldb, BN))
+    if (!make_map(&m[0], op.a_hi, a.M, a.K, op.lda, MT * BM, BKD) ||
+        !make_map(&m[1], op.a_lo, a.M, a.K, op.lda, MT * BM, BKD) ||
+        !make_map(&m[2], op.b_hi, a.N, a.K, op.ldb, BN, BKD) || !make_map(&m[3], op.b_lo, a.N, a.K, op.ldb, BN, BKD))
         return cudaErrorInvalidValue;
     constexpr size_t smem = smem_bytes_mt<BN, MT>();
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, MT, EPI, OUT>,
@@ -883,7 +886,7 @@ cudaError_t launch_split(const TcOperands& op, TcArgs a, int splits, cudaStream_
 template <int EPI, int OUT>
 cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t st) {
     if (splits <= 1) {
-        a.kb_per_split = a.K / BK;
+        a.kb_per_split = a.K / BKD;
         // 129-256 rows (decode batches, the tied head): 256-row tiles, so each
         // B tile crosses from memory once (measured on B200: head over 256
         // rows 250 -> 216-235 us; a prefill FC of 8192 rows slows 300 -> 315
@@ -928,7 +931,7 @@ cudaError_t launch_tc_head(const TcOperands& op, const TcArgs& a, cudaStream_t s
 }
 
 bool tc_gemm_supported(int M, int N, int K, int lda, int ldb) {
-    return M > 0 && N > 0 && K > 0 && K % BK == 0 && lda % 4 == 0 && ldb % 4 == 0 && encode_fn() != nullptr;
+    return M > 0 && N > 0 && K > 0 && K % BKD == 0 && lda % 4 == 0 && ldb % 4 == 0 && encode_fn() != nullptr;
 }
 
 // Split count for a decode-sized matmul, chosen from N and K only, so that a
