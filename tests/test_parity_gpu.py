@@ -134,6 +134,7 @@ def test_small_config1_greedy_128():
         pid, pval = g["prefill_topk_ids"][0], g["prefill_topk_vals"][0]
         ties = argmax_agrees(full, pid, pval)
         assert ties <= 2, ties
+        print(f"config 1 prefill: {ties} of {len(pid)} positions exempt as near-ties")
         assert np.abs(np.take_along_axis(full, pid, 1) - pval).max() <= LOGIT_TOL
 
 
@@ -152,6 +153,8 @@ def test_small_config2_prefill_sweep():
             assert ties <= S * t // 100, (t, ties)
             err = np.abs(np.take_along_axis(logits, pid[:, :t], 2) - pval[:, :t]).max()
             assert err <= LOGIT_TOL, (t, err)
+            print(f"config 2 T={t}: {S * t - ties}/{S * t} positions decided and equal, "
+                  f"{ties} near-tie positions exempt, worst top-k logit error {err:.3g}")
             margin = pval[:, t - 1, 0] - pval[:, t - 1, 1]
             assert np.array_equal(nxt[margin > TIE_MARGIN], pid[:, t - 1, 0][margin > TIE_MARGIN])
             del logits
