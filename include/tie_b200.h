@@ -139,6 +139,15 @@ int model_weight_format(const model *m);
  * stderr. */
 const char *tie_last_device_error(void);
 
+/* The causal prefill attention of the engine (model.c:705-732, the step
+ * between the QKV projection and the output projection) over HOST arrays, for
+ * tests of the kernel alone: qkv is n_seq x T rows of 3 * n_head * 64 floats
+ * (q, k, v of every head, the layout of the fused projection's output) and out
+ * receives n_seq x T rows of n_head * 64. Runs on the current device; returns
+ * MODEL_ERR_ARG for a null pointer or a non-positive size, MODEL_ERR_DEVICE on
+ * a CUDA failure or an expired wait. */
+model_status tie_attention_prefill(const float *qkv, int n_seq, int T, int n_head, float *out);
+
 /* ---- how small decode steps run ------------------------------------------
  * A decode step of at most 8 sequences runs as a chain of per-layer kernels
  * linked by programmatic dependent launch: TIE_STEP_CHAINED, the default

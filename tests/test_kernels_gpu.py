@@ -119,3 +119,40 @@ def test_layernorm_normalize_device():
     ref = oracle.layernorm_normalize(x, 1e-5)
     ulps = np.abs(bits(y).astype(np.int64) - bits(ref).astype(np.int64))
     assert ulps.max() <= 1
+
+
+def attention_f64(qkv, n_head):
+    """Causal attention in float64 (reference model.c:705-732: q.k / sqrt(64),
+    mask, max-subtracted softmax, probability-weighted sum of v)."""
+    n_seq, T, _ = qkv.shape
+    E = n_head * 64
+    q = qkv[..., :E].astype(np.float64).reshape(n_seq, T, n_head, 64)
+    k = qkv[..., E:2 * E].astype(np.float64).reshape(n_seq, T, n_head, 64)
+    v = qkv[..., 2 * E:].astype(np.float64).reshape(n_seq, T, n_head, 64)
+    s = np.einsum("sqhd,skhd->shqk", q, k) / 8.0
+    s = np.where(np.tril(np.ones((T, T), bool)), s, -np.inf)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("shqk,skhd->sqhd", p, v).reshape(n_seq, T, E)
+
+
+@pytest.mark.parametrize("T", [1, 5, 63, 64, 65, 127, 128, 129, 300, 1024])
+def test_prefill_attention_tensor_cores_vs_float64(T):
+    """The tcgen05 prefill attention (3xTF32 products, 64-key blocks, 128-query
+    tiles) against float64, on ragged and tile-aligned lengths."""
+    n_seq, n_head = 2, 3
+    qkv = np.random.default_rng(T).standard_normal((n_seq, T, 3 * n_head * 64)).astype(np.float32)
+    got = tie_b200.attention_prefill(qkv, n_head)
+    ref = attention_f64(qkv, n_head)
+    err = np.abs(got - ref).max()
+    assert err <= 2e-5, err
+
+
+def test_prefill_attention_rows_do_not_depend_on_length():
+    """Row t of a T-token prefill is bit-identical to row t of any longer one
+    (causality; the key blocks past a row's diagonal add exact zeros)."""
+    qkv = np.random.default_rng(7).standard_normal((1, 400, 3 * 64)).astype(np.float32)
+    full = tie_b200.attention_prefill(qkv, 1)
+    for t in (1, 64, 129, 255, 256, 399):
+        part = tie_b200.attention_prefill(qkv[:, :t], 1)
+        assert np.array_equal(bits(part), bits(full[:, :t])), t

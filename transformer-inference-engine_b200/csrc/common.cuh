@@ -193,10 +193,15 @@ cudaError_t launch_kv_store_decode(const float* qkv, const int32_t* lens, int B,
                                    cudaStream_t st);
 
 // Causal attention over T tokens per sequence from the fused qkv activations
-// (prefill, model.c:705-732): out[r, h*D:(h+1)*D].
+// (prefill, model.c:705-732): out[r, h*D:(h+1)*D] (fp32 and/or its tf32 split).
+// The outputs come from the tensor-core kernel (k_tc_attn.cu); with `stats` a
+// second, FFMA pass records the softmax row sums and writes nothing else.
+// `err` (may be null) is set when a bounded wait of the tensor-core kernel expires.
 cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
                                 AttnStats* stats, cudaStream_t st, float* out_hi = nullptr,
-                                float* out_lo = nullptr);
+                                float* out_lo = nullptr, int* err = nullptr);
+cudaError_t launch_tc_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out, float* out_hi,
+                                   float* out_lo, int* err, cudaStream_t st);
 // One query per sequence against its cached positions 0..lens[b] (the new
 // position included), split over position chunks, then combined
 // (model.c:826-850).

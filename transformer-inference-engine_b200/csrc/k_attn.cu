@@ -1,10 +1,11 @@
 // k_attn.cu -- causal attention for GPT-2 (head_dim 64), fp32.
 //
-// Prefill (reference model.c:705-732): per (sequence, head, 64-query tile) one
-// block streams 64-key tiles up to the diagonal through shared memory and keeps
-// an online softmax (running max and sum, rescaled accumulator); the T x T score
-// square is never materialised. Scores are q.k scaled by 1/sqrt(64), the
-// reference's order (dot product, then scale).
+// Prefill (reference model.c:705-732) runs on the tensor cores (k_tc_attn.cu).
+// The FFMA kernel here is the statistics pass of model_collect_attn_stats: per
+// (sequence, head, 64-query tile) one block streams 64-key tiles up to the
+// diagonal through shared memory with an online softmax (running max and sum);
+// the T x T score square is never materialised. Scores are q.k scaled by
+// 1/sqrt(64), the reference's order (dot product, then scale).
 //
 // Decode (reference model.c:826-850): one query per sequence against its cached
 // positions, read through the page table. Positions are split into 64-position
@@ -971,18 +972,16 @@ int attn_decode_kernels(int B) { return B > 16 && B <= kWarpMaxSeqs ? 2 : 1; }
 int attn_decode_max_splits(int capacity) { return (capacity + 15) / 16; }
 
 cudaError_t launch_attn_prefill(const float* qkv, int n_seq, int T, int H, float* out,
-                                AttnStats* stats, cudaStream_t st, float* out_hi, float* out_lo) {
+                                AttnStats* stats, cudaStream_t st, float* out_hi, float* out_lo, int* err) {
     if (T <= 0 || n_seq <= 0) return cudaSuccess;
+    cudaError_t e = launch_tc_attn_prefill(qkv, n_seq, T, H, out, out_hi, out_lo, err, st);
+    if (e != cudaSuccess || !stats) return e;
+    // the statistics pass: same scores and softmax, no outputs
     const size_t smem = (size_t)(BQ * LDS * 3 + BKEY * (BQ + 4)) * sizeof(float);
     const float scale = (float)(1.0 / sqrt((double)D));
     dim3 grid((T + BQ - 1) / BQ, H, n_seq);
-    if (stats) {
-        cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_prefill_kernel<true><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, out_hi, out_lo, stats);
-    } else {
-        cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_prefill_kernel<false><<<grid, 128, smem, st>>>(qkv, T, H, scale, out, out_hi, out_lo, nullptr);
-    }
+    cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attn_prefill_kernel<true><<<grid, 128, smem, st>>>(qkv, T, H, scale, nullptr, nullptr, nullptr, stats);
     return cudaGetLastError();
 }
 

@@ -463,7 +463,7 @@ model_status run_prefill(model* m, int n_seq, int T, kv_cache* cache, int first_
                          m->qkv, nullptr, nullptr, 3 * E)) != MODEL_OK)
             return rc;
         if (cache) LAUNCH(launch_kv_store_prefill(m->qkv, n_seq, T, layer_view(cache, l), first_seq, st));
-        LAUNCH(launch_attn_prefill(m->qkv, n_seq, T, H, nullptr, stats, st, m->attn_hi, m->attn_lo));
+        LAUNCH(launch_attn_prefill(m->qkv, n_seq, T, H, nullptr, stats, st, m->attn_hi, m->attn_lo, m->d_err));
         if ((rc = matmul(m, false, R, attn, E, Mat{w.proj_w, w.proj_hi, w.proj_lo}, E, E, w.proj_b,
                          EPI_BIAS_RESID, m->x, nullptr, nullptr, E)) != MODEL_OK)
             return rc;
@@ -1350,6 +1350,29 @@ void model_layernorm_normalize(const float* x, int n, float eps, float* out) {
     }
 }
 
+model_status tie_attention_prefill(const float* qkv, int n_seq, int T, int n_head, float* out) {
+    if (!qkv || !out || n_seq <= 0 || T <= 0 || n_head <= 0) return MODEL_ERR_ARG;
+    const size_t E = (size_t)n_head * 64, rows = (size_t)n_seq * T;
+    float *dq = nullptr, *dout = nullptr;
+    int* derr = nullptr;
+    int herr = 0;
+    bool ok = cudaMalloc(&dq, rows * 3 * E * 4) == cudaSuccess && cudaMalloc(&dout, rows * E * 4) == cudaSuccess &&
+              cudaMalloc(&derr, sizeof(int)) == cudaSuccess && cudaMemset(derr, 0, sizeof(int)) == cudaSuccess &&
+              cudaMemcpy(dq, qkv, rows * 3 * E * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              launch_attn_prefill(dq, n_seq, T, n_head, dout, nullptr, nullptr, nullptr, nullptr, derr) ==
+                  cudaSuccess &&
+              cudaMemcpy(out, dout, rows * E * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+              cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (!ok) {
+        note_cuda(cudaGetLastError(), "tie_attention_prefill", __LINE__);
+        cudaGetLastError();
+    }
+    cudaFree(dq);
+    cudaFree(dout);
+    cudaFree(derr);
+    return ok && herr == 0 ? MODEL_OK : MODEL_ERR_DEVICE;
+}
+
 // ---------------------------------------------------------------- prefill --
 model_status model_prefill(model* m, const int32_t* ids, size_t T, float* logits, size_t cap) {
     if (!m || !ids || !logits) return MODEL_ERR_ARG;
@@ -1797,7 +1820,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
                     return MODEL_OK;
                 }
             case TIE_KERNEL_PREFILL_ATTENTION:
-                CU(launch_attn_prefill(m->qkv, B, (int)context, H, nullptr, nullptr, st, m->attn_hi, m->attn_lo));
+                CU(launch_attn_prefill(m->qkv, B, (int)context, H, nullptr, nullptr, st, m->attn_hi, m->attn_lo, m->d_err));
                 return MODEL_OK;
             case TIE_KERNEL_PREFILL_FC:
                 return matmul(m, false, (int)R, xb, E, Mat{w.fc_w, w.fc_hi, w.fc_lo}, 4 * E, E, w.fc_b,

@@ -103,6 +103,7 @@ def library():
         "model_token_embedding": (_vp, [_vp]),
         "model_head_weight": (_vp, [_vp]),
         "model_layernorm_normalize": (None, [_fp, C.c_int, C.c_float, _fp]),
+        "tie_attention_prefill": (C.c_int, [_fp, C.c_int, C.c_int, C.c_int, _fp]),
         "model_collect_attn_stats": (None, [_vp, C.c_int]),
         "model_attn_rowsum_range": (None, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                            C.POINTER(C.c_size_t)]),
@@ -492,6 +493,21 @@ def gemm_tiled_bt(A, Bt):
     Cm = np.empty((M, N), np.float32)
     _impl().mul_bt(M, N, K, _fp_of(A), K, _fp_of(Bt), K, _fp_of(Cm), N)
     return Cm
+
+
+def attention_prefill(qkv, n_head):
+    """The engine's causal prefill attention over host qkv [n_seq, T, 3 * n_head * 64]
+    (fp32): returns [n_seq, T, n_head * 64]."""
+    qkv = np.ascontiguousarray(qkv, dtype=np.float32)
+    n_seq, T, w = qkv.shape
+    if w != 3 * n_head * 64:
+        raise ValueError("qkv rows must be 3 * n_head * 64 wide")
+    out = np.empty((n_seq, T, n_head * 64), np.float32)
+    rc = library().tie_attention_prefill(_fp_of(qkv), n_seq, T, n_head, _fp_of(out))
+    if rc != 0:
+        raise RuntimeError(f"tie_attention_prefill: status {rc} "
+                           f"({(library().tie_last_device_error() or b'').decode()})")
+    return out
 
 
 def layernorm_normalize(x, eps):
