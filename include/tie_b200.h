@@ -54,8 +54,28 @@ model_status model_decode_step_greedy(model *m, const int32_t *ids, size_t n_ids
  * model_batch_reserve sizes a paged KV pool and scratch for n_seq sequences of
  * up to `capacity` positions each (pages of KV_CACHE_PAGE_ROWS positions, page
  * tables on the device). It is separate from the single-sequence cache of
- * model_kv_reserve; the batch calls below use only the pool. */
+ * model_kv_reserve; the batch calls below use only the pool. Extends the
+ * reference's kv_cache_create (src/kv_cache.c:150-190) to many sequences. */
 model_status model_batch_reserve(model *m, size_t n_seq, size_t capacity);
+
+/* The same pool over a bounded number of physical pages: n_pages pages of
+ * KV_CACHE_PAGE_ROWS positions per layer (0: enough for every sequence's whole
+ * capacity, which is what model_batch_reserve reserves), plus one scratch page.
+ * No page belongs to a sequence until a batch call needs it: prefill assigns
+ * the pages its prompt covers, each decode step the page its new position
+ * opens, from a free list. A call that finds too few free pages returns
+ * MODEL_ERR_CAPACITY before it launches the step (pages assigned by earlier
+ * steps stay assigned). n_pages above n_seq * ceil(capacity / 16) is
+ * MODEL_ERR_ARG. */
+model_status model_batch_reserve_pages(model *m, size_t n_seq, size_t capacity, size_t n_pages);
+
+/* Returns sequence `seq`'s pages to the pool's free list (a finished sequence,
+ * so that others can grow into its pages). Its positions are then unmapped;
+ * the next prefill that includes it assigns pages again. */
+model_status model_batch_release(model *m, size_t seq);
+
+/* Pages of the pool not assigned to any sequence (0 without a pool). */
+size_t model_batch_free_pages(const model *m);
 
 /* Prefill of n_seq sequences of n_ids tokens each (ids: host, n_seq * n_ids,
  * row-major). Writes every position's keys and values into the pool and sets

@@ -94,3 +94,37 @@ def test_decode_step_batch_refusals(mini_paths):
         assert rc == tie_b200.MODEL_STATUS.index("MODEL_ERR_ARG")  # more sequences than reserved
         rc, _, _ = m.prefill_batch(np.full((2, 4), m.vocab, np.int32), check=False)
         assert rc == tie_b200.MODEL_STATUS.index("MODEL_ERR_RANGE")
+
+
+def test_paged_pool_assigns_pages_as_contexts_grow(mini_paths):
+    """A pool over exactly the pages a generation needs (6 sequences x 49
+    positions = 4 pages each, against 7 each for the full capacity of 100)
+    produces the same ids as a full reservation; released pages are reused by
+    the next batch with results equal to a fresh pool's; a generation that
+    outgrows the pages is refused with MODEL_ERR_CAPACITY."""
+    w, inv, cfg = mini_paths
+    S, T, n_new, cap = 6, 20, 30, 100
+    with tie_b200.Model(w, inv, cfg) as full:
+        prompts = synth.prompt_ids(full.vocab, S, T, seed=51)
+        prompts_b = synth.prompt_ids(full.vocab, S, T, seed=52)
+        full.batch_reserve(S, cap)
+        ref = full.generate_greedy(prompts, n_new)
+        ref_b = full.generate_greedy(prompts_b, n_new)
+    need = S * ((T + n_new - 1 + 15) // 16)
+    with tie_b200.Model(w, inv, cfg) as pm:
+        pm.batch_reserve_pages(S, cap, need)
+        assert pm.batch_free_pages() == need
+        got = pm.generate_greedy(prompts, n_new)
+        assert np.array_equal(got, ref)
+        assert pm.batch_free_pages() == 0
+        for s in range(S):
+            pm.batch_release(s)
+        assert pm.batch_free_pages() == need
+        assert np.array_equal(pm.generate_greedy(prompts_b, n_new), ref_b)
+        for s in range(S):
+            pm.batch_release(s)
+        with pytest.raises(tie_b200.ModelError) as e:
+            pm.generate_greedy(prompts, 60)   # 79 positions: 5 pages each
+        assert tie_b200.MODEL_STATUS[e.value.status] == "MODEL_ERR_CAPACITY"
+        with pytest.raises(tie_b200.ModelError):
+            pm.batch_reserve_pages(S, cap, S * 7 + 1)   # more pages than the sequences can hold

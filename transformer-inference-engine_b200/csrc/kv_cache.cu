@@ -18,11 +18,11 @@ cudaError_t copy_any(void* dst, const void* src, size_t bytes) {
     return cudaDeviceSynchronize();
 }
 
-static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, bool contiguous,
+static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, bool contiguous, int n_pages,
                              kv_cache** out) {
     if (!out) return KV_ERR_ARG;
     *out = nullptr;
-    if (n_layer <= 0 || n_embd <= 0 || capacity <= 0 || n_seq <= 0) return KV_ERR_ARG;
+    if (n_layer <= 0 || n_embd <= 0 || capacity <= 0 || n_seq <= 0 || n_pages < 0) return KV_ERR_ARG;
     kv_cache* c = new (std::nothrow) kv_cache();
     if (!c) return KV_ERR_NOMEM;
     c->n_layer = n_layer;
@@ -32,13 +32,20 @@ static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, b
     c->contiguous = contiguous;
     c->pages_per_seq = (capacity + KV_CACHE_PAGE_ROWS - 1) / KV_CACHE_PAGE_ROWS;
     // One sequence: exactly `capacity` rows (the last page may be partial, and
-    // no position reaches past capacity). A pool: whole pages per sequence.
-    c->rows = contiguous ? (size_t)capacity
-                         : (size_t)n_seq * c->pages_per_seq * KV_CACHE_PAGE_ROWS;
+    // no position reaches past capacity), pages in order. A pool: n_pages
+    // assignable pages plus the scratch page unmapped entries point at.
+    if (!contiguous && n_pages == 0) n_pages = n_seq * c->pages_per_seq;
+    c->rows = contiguous ? (size_t)capacity : (size_t)(n_pages + 1) * KV_CACHE_PAGE_ROWS;
     c->bytes = (size_t)n_layer * 2u * c->rows * (size_t)n_embd * sizeof(float);
     const size_t per = (size_t)n_layer * c->rows * n_embd * sizeof(float);
-    std::vector<int> table((size_t)n_seq * c->pages_per_seq);
-    for (size_t i = 0; i < table.size(); ++i) table[i] = (int)i;  // pages in order
+    const size_t entries = (size_t)n_seq * c->pages_per_seq;
+    std::vector<int> table(entries);
+    if (contiguous) {
+        for (size_t i = 0; i < entries; ++i) table[i] = (int)i;   // pages in order
+    } else {
+        c->pages = tie::PageTable(n_seq, capacity, n_pages);
+        table = c->pages.device_view();                          // all entries on the scratch page
+    }
     // A one-sequence cache is managed memory: its kv_cache_keys/values/*_row
     // addresses are usable on the host too (the reference's callers read rows
     // through them between calls), and its pages live in device memory while
@@ -47,10 +54,9 @@ static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, b
         return contiguous ? cudaMallocManaged(p, per, cudaMemAttachGlobal) : cudaMalloc(p, per);
     };
     if (alloc(&c->k) != cudaSuccess || alloc(&c->v) != cudaSuccess ||
-        cudaMalloc(&c->d_page_table, table.size() * sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->d_page_table, entries * sizeof(int)) != cudaSuccess ||
         cudaMemset(c->k, 0, per) != cudaSuccess || cudaMemset(c->v, 0, per) != cudaSuccess ||
-        cudaMemcpy(c->d_page_table, table.data(), table.size() * sizeof(int),
-                   cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->d_page_table, table.data(), entries * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
         cudaGetLastError();
         kv_cache_destroy(c);
@@ -60,8 +66,36 @@ static kv_status create_impl(int n_layer, int n_embd, int n_seq, int capacity, b
     return KV_OK;
 }
 
-kv_status kv_pool_create(int n_layer, int n_embd, int n_seq, int capacity, kv_cache** out) {
-    return create_impl(n_layer, n_embd, n_seq, capacity, false, out);
+kv_status kv_pool_create(int n_layer, int n_embd, int n_seq, int capacity, int n_pages, kv_cache** out) {
+    return create_impl(n_layer, n_embd, n_seq, capacity, false, n_pages, out);
+}
+
+kv_status kv_pool_map(kv_cache* c, int n_seq, int length, cudaStream_t st) {
+    if (!c || c->contiguous || n_seq < 0 || n_seq > c->n_seq || length < 0) return KV_ERR_ARG;
+    if (length > c->capacity) return KV_ERR_CAPACITY;
+    kv_status rc = KV_OK;
+    for (int s = 0; s < n_seq; ++s)
+        if (!c->pages.map(s, length)) {
+            rc = KV_ERR_CAPACITY;
+            break;
+        }
+    if (c->pages.dirty()) {
+        // the host view is copied before the call returns (pageable source),
+        // and the copy is ordered before every later kernel on `st`
+        const std::vector<int>& view = c->pages.device_view();
+        if (cudaMemcpyAsync(c->d_page_table, view.data(), view.size() * sizeof(int), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return KV_ERR_NOMEM;
+        }
+    }
+    return rc;
+}
+
+kv_status kv_pool_release(kv_cache* c, int seq) {
+    if (!c || c->contiguous || seq < 0 || seq >= c->n_seq) return KV_ERR_ARG;
+    c->pages.release(seq);
+    return KV_OK;
 }
 
 }  // namespace tie
@@ -84,7 +118,7 @@ size_t kv_cache_footprint_for(int n_layer, int n_embd, int capacity) {
 }
 
 kv_status kv_cache_create(int n_layer, int n_embd, int capacity, kv_cache** out) {
-    return tie::create_impl(n_layer, n_embd, 1, capacity, true, out);
+    return tie::create_impl(n_layer, n_embd, 1, capacity, true, 0, out);
 }
 
 void kv_cache_destroy(kv_cache* c) {

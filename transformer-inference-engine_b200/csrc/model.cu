@@ -1471,13 +1471,39 @@ size_t model_weight_device_bytes(const model* m) {
 }
 uint64_t model_kernel_launches(const model* m) { return m ? m->launches : 0; }
 
+// Pages covering positions [0, length) for the pool's sequences [0, n_seq),
+// assigned from the pool's free pages, the device table updated on the model's
+// stream (before the kernels that follow).
+static model_status map_pages(model* m, size_t n_seq, size_t length) {
+    const kv_status ks = kv_pool_map(m->pool, (int)n_seq, (int)length, m->st);
+    if (ks == KV_OK) return MODEL_OK;
+    if (ks == KV_ERR_CAPACITY) return MODEL_ERR_CAPACITY;
+    if (ks == KV_ERR_NOMEM) {
+        note_cuda(cudaErrorMemoryAllocation, "page table update", __LINE__);
+        return MODEL_ERR_DEVICE;
+    }
+    return MODEL_ERR_ARG;
+}
+
 model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
+    return model_batch_reserve_pages(m, n_seq, capacity, 0);
+}
+
+model_status model_batch_reserve_pages(model* m, size_t n_seq, size_t capacity, size_t n_pages) {
     if (!m || n_seq == 0 || capacity == 0) return MODEL_ERR_ARG;
     if ((int)capacity > m->cfg.n_ctx) return MODEL_ERR_RANGE;
     if (n_seq > 1024) return MODEL_ERR_ARG;
-    if (!m->pool || m->pool->n_seq < (int)n_seq || m->pool->capacity < (int)capacity) {
+    const size_t per_seq = (capacity + KV_CACHE_PAGE_ROWS - 1) / KV_CACHE_PAGE_ROWS;
+    if (n_pages > n_seq * per_seq) return MODEL_ERR_ARG;
+    const int want_pages = (int)(n_pages ? n_pages : n_seq * per_seq);
+    // a new pool unless the current one covers the request: as many sequences,
+    // as long, and exactly n_pages pages (n_pages given) or at least a full
+    // reservation's pages (n_pages 0)
+    if (!m->pool || m->pool->n_seq < (int)n_seq || m->pool->capacity < (int)capacity ||
+        (n_pages ? m->pool->pages.n_pages() != want_pages : m->pool->pages.n_pages() < want_pages)) {
         kv_cache* fresh = nullptr;
-        kv_status ks = kv_pool_create(m->cfg.n_layer, m->cfg.n_embd, (int)n_seq, (int)capacity, &fresh);
+        kv_status ks = kv_pool_create(m->cfg.n_layer, m->cfg.n_embd, (int)n_seq, (int)capacity, (int)n_pages,
+                                      &fresh);
         if (ks != KV_OK) return ks == KV_ERR_NOMEM ? MODEL_ERR_NOMEM : MODEL_ERR_ARG;
         drop_graphs(m);
         kv_cache_destroy(m->pool);
@@ -1490,6 +1516,15 @@ model_status model_batch_reserve(model* m, size_t n_seq, size_t capacity) {
     return ensure_logits(m, n_seq);
 }
 
+model_status model_batch_release(model* m, size_t seq) {
+    if (!m || !m->pool || seq >= (size_t)m->pool->n_seq) return MODEL_ERR_ARG;
+    return kv_pool_release(m->pool, (int)seq) == KV_OK ? MODEL_OK : MODEL_ERR_ARG;
+}
+
+size_t model_batch_free_pages(const model* m) {
+    return m && m->pool ? (size_t)m->pool->pages.free_pages() : 0;
+}
+
 static model_status batch_prefill_impl(model* m, size_t n_seq, size_t T, float* logits_host,
                                        int32_t* next_host, bool host_ids, const int32_t* ids) {
     const int V = m->cfg.vocab_size;
@@ -1499,6 +1534,7 @@ static model_status batch_prefill_impl(model* m, size_t n_seq, size_t T, float* 
     } else {
         CU(cudaMemcpyAsync(m->d_ids, ids, n_seq * T * sizeof(int32_t), cudaMemcpyDeviceToDevice, m->st));
     }
+    if ((rc = map_pages(m, n_seq, T)) != MODEL_OK) return rc;
     if ((rc = run_prefill(m, (int)n_seq, (int)T, m->pool, 0)) != MODEL_OK) return rc;
     if (logits_host) {
         if ((rc = ensure_logits(m, n_seq * T)) != MODEL_OK) return rc;
@@ -1547,6 +1583,7 @@ model_status model_decode_step_batch(model* m, const int32_t* ids, size_t n_seq,
     if ((rc = stats_begin(m)) != MODEL_OK) return rc;
     std::vector<int32_t> lens(n_seq, (int32_t)m->pool->length);
     if ((rc = set_slot_state(m, n_seq, ids, lens.data())) != MODEL_OK) return rc;
+    if ((rc = map_pages(m, n_seq, (size_t)m->pool->length + 1)) != MODEL_OK) return rc;
     if ((rc = decode_step(m, (int)n_seq, m->pool, false, nullptr, 0)) != MODEL_OK) return rc;
     if (logits)
         CU(cudaMemcpyAsync(logits, m->logits, n_seq * (size_t)m->cfg.vocab_size * sizeof(float),
@@ -1587,8 +1624,12 @@ static model_status generate_impl(model* m, const int32_t* prompts, size_t n_seq
     CU(cudaMemcpyAsync(m->d_lens, m->h_small, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
     CU(cudaMemsetAsync(m->d_step, 0, sizeof(int32_t), m->st));
     LAUNCH(launch_step_advance(m->d_next, m->d_tokens, m->d_lens, d_out, (int)n_new, m->d_step, (int)n_seq, m->st));
-    for (size_t g = 1; g < n_new; ++g)
+    // step g writes position T + g - 1 and reads 0 .. T + g - 1: its pages are
+    // assigned before it is launched (a new page every 16 steps)
+    for (size_t g = 1; g < n_new; ++g) {
+        if ((rc = map_pages(m, n_seq, T + g)) != MODEL_OK) return rc;
         if ((rc = decode_step(m, (int)n_seq, m->pool, true, d_out, (int)n_new)) != MODEL_OK) return rc;
+    }
     if (host)
         CU(cudaMemcpyAsync(out_ids, d_out, n_seq * n_new * sizeof(int32_t), cudaMemcpyDeviceToHost, m->st));
     m->pool->length = (int)(T + n_new - 1);
@@ -1619,6 +1660,7 @@ model_status model_step_trace(model* m, size_t rows, size_t context, uint64_t* o
     if (!out || cap < ev * G) return MODEL_ERR_CAPACITY;
     std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
     if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    if ((rc = map_pages(m, rows, context)) != MODEL_OK) return rc;
     unsigned long long* d = nullptr;
     CU(cudaMalloc(&d, ev * G * sizeof(unsigned long long)));
     CU(cudaMemsetAsync(d, 0, ev * G * sizeof(unsigned long long), m->st));
@@ -1669,6 +1711,7 @@ model_status model_stream_trace(model* m, size_t rows, size_t context, uint64_t*
     if (rc != MODEL_OK) return rc;
     std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
     if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    if ((rc = map_pages(m, rows, context)) != MODEL_OK) return rc;
     unsigned long long* d = nullptr;
     CU(cudaMalloc(&d, per * kernels * sizeof(unsigned long long)));
     CU(cudaMemsetAsync(d, 0, per * kernels * sizeof(unsigned long long), m->st));
@@ -1715,6 +1758,7 @@ model_status model_time_kernel(model* m, int kernel, size_t rows, size_t context
     // deterministic, finite contents for every operand
     std::vector<int32_t> lens(rows, (int32_t)context - 1), toks(rows, 1);
     if ((rc = set_slot_state(m, rows, toks.data(), lens.data())) != MODEL_OK) return rc;
+    if ((rc = map_pages(m, rows, context)) != MODEL_OK) return rc;
     const size_t R = kernel >= TIE_KERNEL_PREFILL_ATTENTION ? rows * context : rows;
     CU(cudaMemsetAsync(m->qkv, 0, R * 3 * E * sizeof(float), st));
     CU(cudaMemsetAsync(m->x, 0, R * E * sizeof(float), st));

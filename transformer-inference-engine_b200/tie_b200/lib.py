@@ -114,6 +114,9 @@ def library():
         "model_kernel_launches": (C.c_uint64, [_vp]),
         "model_decode_step_greedy": (C.c_int, [_vp, _ip, C.c_size_t, _ip]),
         "model_batch_reserve": (C.c_int, [_vp, C.c_size_t, C.c_size_t]),
+        "model_batch_reserve_pages": (C.c_int, [_vp, C.c_size_t, C.c_size_t, C.c_size_t]),
+        "model_batch_release": (C.c_int, [_vp, C.c_size_t]),
+        "model_batch_free_pages": (C.c_size_t, [_vp]),
         "model_prefill_batch": (C.c_int, [_vp, _ip, C.c_size_t, C.c_size_t, _fp, C.c_size_t, _ip]),
         "model_decode_step_batch": (C.c_int, [_vp, _ip, C.c_size_t, _fp, C.c_size_t, _ip]),
         "model_generate_greedy": (C.c_int, [_vp, _ip, C.c_size_t, C.c_size_t, C.c_size_t, _ip]),
@@ -397,6 +400,17 @@ class Model:
 
     def batch_reserve(self, n_seq, capacity):
         return _chk(library().model_batch_reserve(self.h, n_seq, capacity), "model_batch_reserve")
+
+    def batch_reserve_pages(self, n_seq, capacity, n_pages):
+        """A batch pool over n_pages physical KV pages, assigned as contexts grow."""
+        return _chk(library().model_batch_reserve_pages(self.h, n_seq, capacity, n_pages),
+                    "model_batch_reserve_pages")
+
+    def batch_release(self, seq):
+        return _chk(library().model_batch_release(self.h, seq), "model_batch_release")
+
+    def batch_free_pages(self) -> int:
+        return library().model_batch_free_pages(self.h)
 
     def prefill_batch(self, ids, want_logits=False, check=True):
         ids = _ids(ids)
