@@ -499,7 +499,17 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
         const int row = m0 + r, col = n0 + 4 * c4;
         if (row >= p.M || col >= p.N) continue;
         const uint32_t local = smem_u32(red + (size_t)r * kRedLd + 4 * c4);
-        // every split's value in flight at once, then summed in split order
+        const size_t o = (size_t)row * p.ldc + col;
+        // the epilogue's operands (bias, residual) and every split's value in
+        // flight at once -- one round trip per item, not one per operand --
+        // then the splits summed in split order
+        float bv[4] = {0.f, 0.f, 0.f, 0.f}, rv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (col + e < p.N) {
+                if constexpr (EPI != EPI_STORE) bv[e] = __ldg(p.bias + col + e);
+                if constexpr (EPI == EPI_BIAS_RESID) rv[e] = p.C[o + e];
+            }
         float4 v[kMaxSplits];
 #pragma unroll
         for (int s = 0; s < kMaxSplits; ++s)
@@ -514,11 +524,14 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
                 acc.w = __fadd_rn(acc.w, v[s].w);
             }
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-        const size_t o = (size_t)row * p.ldc + col;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (col + e >= p.N) break;
-            const float y = apply_epi<EPI>(a4[e], p.bias, col + e, p.C + o + e);
+            // apply_epi's arithmetic on the operands loaded above
+            float y = a4[e];
+            if constexpr (EPI == EPI_BIAS) y = __fadd_rn(y, bv[e]);
+            else if constexpr (EPI == EPI_BIAS_GELU) y = gelu_new_ref(__fadd_rn(y, bv[e]));
+            else if constexpr (EPI == EPI_BIAS_RESID) y = __fadd_rn(rv[e], __fadd_rn(y, bv[e]));
             if constexpr (OUT == TC_OUT_F32 || OUT == TC_OUT_F32_HILO) p.C[o + e] = y;
             if constexpr (OUT == TC_OUT_HILO || OUT == TC_OUT_F32_HILO) {
                 const float h = tf32_hi(y);
