@@ -110,15 +110,6 @@ __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// hi = x rounded to tf32 (nearest, ties away from zero) with integer
-// operations: half a tf32 ulp (bit 12) is added to the magnitude bits and the
-// low 13 bits are cleared; a carry out of the mantissa moves into the exponent,
-// which is the correct rounding up to the next binade. Finite inputs only (the
-// scores, probabilities and activations here are finite).
-__device__ __forceinline__ float tf32_hi_int(float x) {
-    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
 // A 16-byte read-only global load that stays where it is written: volatile,
 // so the compiler neither sinks it to the first use of its registers nor moves
 // it across the barrier waits (the loaders fetch the next key block's rows

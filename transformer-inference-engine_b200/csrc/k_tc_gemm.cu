@@ -563,8 +563,14 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_con
 // depend on the batch it decodes in): the 3xTF32 MMAs of tc_gemm_kernel into
 // TMEM, fed by TMA through a deep ring of 128-byte-swizzled k-blocks (32
 // columns), the weight tiles of the first stages requested before
-// griddepcontrol.wait. The epilogue warps read the accumulator back and store
-// it transposed: for each activation row, a warp writes 32 consecutive logits.
+// griddepcontrol.wait. The weights arrive as fp32 (one k-block of 128 rows is
+// 16 KB); the epilogue warps, idle until the accumulator is complete, split
+// each landed weight tile in shared memory into its tf32 hi half (in place) and
+// lo half (the tile's second slot) -- the split the MMAs need, bit for bit the
+// one stored for the other matmuls -- so the weights cross from memory once,
+// at half the bytes of streaming a stored split. Then the epilogue warps read
+// the accumulator back and store it transposed: for each activation row, a
+// warp writes 32 consecutive logits.
 constexpr int kDecStagesMax = 8;
 constexpr int kHeadPrefetch = 8;   // k-blocks of weights requested into L2 ahead of the ring
 constexpr uint32_t kDecTileW = BM * 128;   // one k-block of 128 weight rows
@@ -572,18 +578,18 @@ constexpr uint32_t kDecTileW = BM * 128;   // one k-block of 128 weight rows
 __host__ __device__ constexpr uint32_t dec_stage_bytes(int nb) { return 2u * kDecTileW + 2u * (uint32_t)nb * 128u; }
 
 __global__ void __launch_bounds__(THREADS, 1)
-tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
-               const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, TcArgs p,
-               int nb, int S, int tcols) {
+tc_head_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx_hi,
+               const __grid_constant__ CUtensorMap tx_lo, TcArgs p, int nb, int S, int tcols) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t SB = dec_stage_bytes(nb);
     const uint32_t tileX = (uint32_t)nb * 128u;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (uint32_t)S * SB);
-    uint64_t* full = bars;                   // [S]  TMA -> MMA
-    uint64_t* empty = bars + kDecStagesMax;  // [S]  MMA -> TMA
-    uint64_t* tfull = bars + 2 * kDecStagesMax;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kDecStagesMax + 1);
+    uint64_t* full = bars;                       // [S]  TMA -> splitters
+    uint64_t* empty = bars + kDecStagesMax;      // [S]  MMA -> TMA
+    uint64_t* split = bars + 2 * kDecStagesMax;  // [S]  splitters -> MMA (128 arrivals)
+    uint64_t* tfull = bars + 3 * kDecStagesMax;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kDecStagesMax + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -594,6 +600,7 @@ tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant_
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 1);
+            mbar_init(smem_u32(&split[s]), 128);
         }
         mbar_init(smem_u32(&tfull[0]), 1);
         *abort_flag = 0;
@@ -630,22 +637,20 @@ tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant_
         if (lane == 0) {
             const int pre = min(S, nkb);
             // weights first: no earlier kernel writes them
+            const uint32_t tx_bytes = kDecTileW + 2u * tileX;   // fp32 weights, x hi and lo
             for (int kb = 0; kb < pre; ++kb) {
                 const uint32_t base = smem_u32(smem + kb * SB);
                 const uint32_t fb = smem_u32(&full[kb]);
-                mbar_expect_tx(fb, SB);
-                tma_load_2d(base, &tw_hi, fb, kb * BKD, n0);
-                tma_load_2d(base + kDecTileW, &tw_lo, fb, kb * BKD, n0);
+                mbar_expect_tx(fb, tx_bytes);
+                tma_load_2d(base, &tw, fb, kb * BKD, n0);
             }
             // weight boxes kHeadPrefetch k-blocks ahead of the ring go to L2
             // when the ring is two stages deep (129-256 rows; measured on
             // B200: 256 rows 162 -> 138 us; with the four-stage ring of 32 rows
-            // the prefetches slowed it 74 -> 82 us)
+            // the prefetches slowed it 74 -> 82 us, and a prefetch of the CTA's
+            // whole contiguous weight slab slowed every size, 32 rows 74 -> 86)
             const int pf = S <= 2 ? kHeadPrefetch : 0;
-            for (int kb = pre; kb < min(nkb, pre + pf); ++kb) {
-                tma_prefetch_2d(&tw_hi, kb * BKD, n0);
-                tma_prefetch_2d(&tw_lo, kb * BKD, n0);
-            }
+            for (int kb = pre; kb < min(nkb, pre + pf); ++kb) tma_prefetch_2d(&tw, kb * BKD, n0);
             grid_dep_wait();
             for (int kb = 0; kb < pre; ++kb) {
                 const uint32_t base = smem_u32(smem + kb * SB);
@@ -659,15 +664,11 @@ tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant_
                 if (!wait(smem_u32(&empty[s]), ((kb / S) & 1u) ^ 1u)) break;
                 const uint32_t base = smem_u32(smem + s * SB);
                 const uint32_t fb = smem_u32(&full[s]);
-                mbar_expect_tx(fb, SB);
-                tma_load_2d(base, &tw_hi, fb, kb * BKD, n0);
-                tma_load_2d(base + kDecTileW, &tw_lo, fb, kb * BKD, n0);
+                mbar_expect_tx(fb, tx_bytes);
+                tma_load_2d(base, &tw, fb, kb * BKD, n0);
                 tma_load_2d(base + 2 * kDecTileW, &tx_hi, fb, kb * BKD, 0);
                 tma_load_2d(base + 2 * kDecTileW + tileX, &tx_lo, fb, kb * BKD, 0);
-                if (pf && kb + pf < nkb) {
-                    tma_prefetch_2d(&tw_hi, (kb + pf) * BKD, n0);
-                    tma_prefetch_2d(&tw_lo, (kb + pf) * BKD, n0);
-                }
+                if (pf && kb + pf < nkb) tma_prefetch_2d(&tw, (kb + pf) * BKD, n0);
             }
             // every copy this thread started has landed before the CTA may exit
             for (int j = kb > S ? kb - S : 0; j < kb; ++j) {
@@ -683,7 +684,7 @@ tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant_
                                    ((uint32_t)(BM >> 4) << 24);
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % S;
-                if (!wait(smem_u32(&full[s]), (kb / S) & 1u)) break;
+                if (!wait(smem_u32(&split[s]), (kb / S) & 1u)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t base = smem_u32(smem + s * SB);
 #pragma unroll
@@ -702,9 +703,30 @@ tc_head_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant_
             mma_commit(smem_u32(&tfull[0]));
         }
     } else {
-        // ------------------------------------------------------- epilogue
+        // ---------------------------- weight splitters, then the epilogue
+        // Each landed weight tile (16 KB, 128-byte-swizzled) becomes its hi half
+        // in place and its lo half in the tile's second slot; the swizzle is a
+        // function of the position only, so the halves keep the tile's layout.
+        const int t = threadIdx.x - 64;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % S;
+            if (!wait(smem_u32(&full[s]), (kb / S) & 1u)) { ok = false; break; }
+            float4* w = reinterpret_cast<float4*>(smem + s * SB);
+#pragma unroll
+            for (int i = 0; i < (int)(kDecTileW / 16) / 128; ++i) {
+                const int e = t + 128 * i;
+                const float4 v = w[e];
+                const float4 h = make_float4(tf32_hi_int(v.x), tf32_hi_int(v.y), tf32_hi_int(v.z), tf32_hi_int(v.w));
+                w[e] = h;
+                w[e + kDecTileW / 16] = make_float4(__fsub_rn(v.x, h.x), __fsub_rn(v.y, h.y), __fsub_rn(v.z, h.z),
+                                                    __fsub_rn(v.w, h.w));
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(smem_u32(&split[s]));
+        }
         const int q = warp & 3;                // TMEM lane quarter: vocabulary rows n0 + q * 32 + lane
-        const bool ok = wait(smem_u32(&tfull[0]), 0);
+        ok = wait(smem_u32(&tfull[0]), 0) && ok;
         asm volatile("tcgen05.fence::after_thread_sync;");
         const int col = n0 + q * 32 + lane;
         for (int c = 0; c < nb / 32 + (nb % 32 ? 1 : 0); ++c) {
@@ -851,9 +873,9 @@ cudaError_t launch_epi(const TcOperands& op, TcArgs a, int splits, cudaStream_t 
 cudaError_t launch_head(const TcOperands& op, TcArgs a, cudaStream_t st) {
     const int nb = (a.M + 15) / 16 * 16;
     if (nb < 16 || nb > 256) return cudaErrorInvalidValue;
-    CUtensorMap m[4];
-    if (!make_map(&m[0], op.b_hi, a.N, a.K, op.ldb, BM, BKD) || !make_map(&m[1], op.b_lo, a.N, a.K, op.ldb, BM, BKD) ||
-        !make_map(&m[2], op.a_hi, a.M, a.K, op.lda, nb, BKD) || !make_map(&m[3], op.a_lo, a.M, a.K, op.lda, nb, BKD))
+    CUtensorMap m[3];
+    if (!op.b_f32 || !make_map(&m[0], op.b_f32, a.N, a.K, op.ldb, BM, BKD) ||
+        !make_map(&m[1], op.a_hi, a.M, a.K, op.lda, nb, BKD) || !make_map(&m[2], op.a_lo, a.M, a.K, op.lda, nb, BKD))
         return cudaErrorInvalidValue;
     // one CTA per SM: a deep ring keeps several stages' copies in flight
     const uint32_t sb = dec_stage_bytes(nb);
@@ -868,7 +890,7 @@ cudaError_t launch_head(const TcOperands& op, TcArgs a, cudaStream_t st) {
         configured = true;
     }
     cudaError_t e = launch_pdl(tc_head_kernel, dim3((a.N + BM - 1) / BM), dim3(THREADS), smem, st, m[0], m[1], m[2],
-                               m[3], a, nb, S, tcols);
+                               a, nb, S, tcols);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 

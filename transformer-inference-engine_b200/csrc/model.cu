@@ -406,7 +406,9 @@ model_status matmul(model* m, bool decode, int rows, Mat x, int ldx, Mat w, int 
     a.err = m->d_err;
     const int out = y_hi ? (y ? TC_OUT_F32_HILO : TC_OUT_HILO) : TC_OUT_F32;
     if (decode && epi == EPI_STORE && out == TC_OUT_F32 && rows <= kHeadTileRows) {
-        // the tied head of a decode step: the vocabulary as the MMA's 128-row operand
+        // the tied head of a decode step: the vocabulary as the MMA's 128-row
+        // operand, read as fp32 and split in shared memory
+        op.b_f32 = w.f;
         LAUNCH(launch_tc_head(op, a, st));
         return MODEL_OK;
     }

@@ -22,6 +22,7 @@ struct TcOperands {
     const float* b_hi;
     const float* b_lo;
     int ldb;
+    const float* b_f32 = nullptr;   // B itself (the tied head reads it and splits in shared memory)
 };
 
 struct TcArgs {
@@ -41,6 +42,15 @@ __device__ __forceinline__ float tf32_hi(float x) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
+}
+
+// The same rounding with integer operations (round to nearest, ties away
+// from zero, at the 13th mantissa bit: half a tf32 ulp is added to the
+// magnitude bits and the low 13 bits cleared; a carry out of the mantissa moves
+// into the exponent). Equal to tf32_hi for every finite x; it runs on the
+// integer pipe instead of the conversion unit.
+__device__ __forceinline__ float tf32_hi_int(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 bool tc_gemm_supported(int M, int N, int K, int lda, int ldb);
