@@ -128,3 +128,17 @@ def test_paged_pool_assigns_pages_as_contexts_grow(mini_paths):
         assert tie_b200.MODEL_STATUS[e.value.status] == "MODEL_ERR_CAPACITY"
         with pytest.raises(tie_b200.ModelError):
             pm.batch_reserve_pages(S, cap, S * 7 + 1)   # more pages than the sequences can hold
+
+
+def test_prefill_rows_do_not_depend_on_the_batch(m):
+    """A prefill of 8 x 128 = 1024 rows gives every sequence's logits bit for
+    bit as its own 128-row prefill: LayerNorm, the tensor-core matmuls (a row's
+    sums do not depend on the tile it lands in) and attention compute each row
+    independently of the batch."""
+    S, T = 8, 128
+    prompts = synth.prompt_ids(m.vocab, S, T, seed=61)
+    m.batch_reserve(S, T)
+    _, full = m.prefill_batch(prompts, want_logits=True)
+    for s in (0, 3, 7):
+        _, one = m.prefill_batch(prompts[s:s + 1], want_logits=True)
+        assert np.array_equal(bits(one[0]), bits(full[s])), s
