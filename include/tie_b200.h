@@ -240,8 +240,9 @@ model_status model_step_trace(model *m, size_t rows, size_t context, uint64_t *o
  * partial maxima live in a fixed 512 KiB array inside the library, present on
  * every GPU that loads it until the process exits; nothing is allocated per
  * call. The array's device address is looked up on the first call made on each
- * device (with that device current). Every call shares the array, so calls that
- * overlap on the GPU race on it. */
+ * device (with that device current); make that first call before any stream
+ * capture. Every call shares the array, so calls that overlap on the GPU race
+ * on it. */
 model_status tie_head_argmax_noalloc(const float *x, int ldx, const float *w, int ldw, int rows,
                                      int vocab, int k, float *logits, int ldl, int32_t *next,
                                      void *stream);

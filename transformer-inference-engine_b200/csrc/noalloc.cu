@@ -13,7 +13,8 @@
 // The array lives in every GPU that loads this library, for the life of the
 // process (512 KiB). Its address is looked up on the first call made with a
 // device current (cudaGetSymbolAddress, which also makes the device's primary
-// context current if it is not yet). The address is kept together with the context it belongs to and
+// context current if it is not yet); that first call on a device should come
+// before any stream capture. The address is kept together with the context it belongs to and
 // looked up again when a call finds another context current (after
 // cudaDeviceReset, for instance). All calls share the one array: two calls
 // that overlap on the GPU (different streams, or different host threads on one
